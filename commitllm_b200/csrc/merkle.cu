@@ -1,0 +1,591 @@
+// Merkle kernels: KV leaves fused with their subtree reduction, generic trees
+// over given leaves, and openings.
+//
+// Tree semantics follow crates/verilm-core/src/merkle.rs:
+//   build_tree (11-48): level 0 is the leaves zero-padded to the next power of
+//   two; parent = hash_pair(left, right) = SHA256(left || right) (118-123);
+//   nodes are stored level-concatenated bottom-up, root last.
+//   prove (79-99): siblings bottom-up, sibling = idx ^ 1 at each level.
+//
+// Work split: a CTA owns an aligned chunk of up to 128 leaves of one tree
+// (one thread per leaf).  It hashes the leaves, reduces the chunk to its
+// subtree root in shared memory, and counts itself done on the tree's
+// counter; the CTA that completes a tree's last chunk finishes the levels
+// above the chunks (threadfence reduction, no waiting anywhere).  Chunks that
+// hold only zero padding are never launched: their subtree root is the
+// constant Z_k (Z_0 = 0^32, Z_{k+1} = hash_pair(Z_k, Z_k)), which is exactly
+// what build_tree computes for them.
+#include "sha256_core.cuh"
+#include "sha256_stream.cuh"
+#include "vc_internal.h"
+
+namespace vc {
+
+__host__ __device__ __forceinline__ int64_t level_off(int lp, int k) {
+  // Nodes before level k in a tree with 2^lp leaves: sum_{i<k} 2^(lp-i).
+  return (int64_t(2) << lp) - (int64_t(2) << (lp - k));
+}
+
+__device__ __forceinline__ void store_z(uint8_t* p, const uint32_t* z) {
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = z[i];
+  store_digest(p, h);
+}
+
+// ---------------------------------------------------------------------------
+// Subtree of one chunk, in shared memory.  sd[w][i] is word w of leaf i.
+// ---------------------------------------------------------------------------
+template <int NT>
+__device__ __forceinline__ void chunk_reduce(uint32_t (*sd)[NT], int kc, uint8_t* tnodes, int lp,
+                                             int64_t chunk) {
+  const int tid = threadIdx.x;
+  for (int k = 0; k < kc; ++k) {
+    const int half = 1 << (kc - k - 1);
+    uint32_t out[8];
+    if (tid < half) {
+      uint32_t l[8], r[8];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) { l[w] = sd[w][2 * tid]; r[w] = sd[w][2 * tid + 1]; }
+      hash_pair(l, r, out);
+    }
+    __syncthreads();
+    if (tid < half) {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sd[w][tid] = out[w];
+      if (tnodes) store_digest(tnodes + (level_off(lp, k + 1) + (chunk << (kc - k - 1)) + tid) * 32, out);
+    }
+    __syncthreads();
+  }
+}
+
+// Levels above the chunks, run by the CTA that finished a tree's last chunk.
+// tnodes: the tree's node array (nullptr in roots-only mode, where tcroot
+// holds the chunk roots and is reduced in place).
+template <int NT>
+__device__ void finish_tree(uint8_t* tnodes, uint8_t* tcroot, int64_t n, int lp, int kc,
+                            int n_chunks, const uint32_t* Z, uint8_t* root_out) {
+  const int tid = threadIdx.x;
+  if (tnodes) {
+    // Zero-padding chunks: every node of theirs at levels 0..kc is Z_k.
+    const int64_t m = int64_t(1) << (lp - kc);
+    for (int k = 0; k <= kc; ++k) {
+      const int64_t per = int64_t(1) << (kc - k);
+      uint8_t* lvl = tnodes + level_off(lp, k) * 32;
+      for (int64_t i = int64_t(n_chunks) * per + tid; i < m * per; i += NT) store_z(lvl + i * 32, Z + 8 * k);
+    }
+  }
+  for (int k = kc; k < lp; ++k) {
+    const int64_t real_k = (n + (int64_t(1) << k) - 1) >> k;
+    const int64_t real_k1 = (n + (int64_t(1) << (k + 1)) - 1) >> (k + 1);
+    const int64_t half = int64_t(1) << (lp - k - 1);
+    const uint8_t* src = tnodes ? tnodes + level_off(lp, k) * 32 : tcroot;
+    uint8_t* dst = tnodes ? tnodes + level_off(lp, k + 1) * 32 : tcroot;
+    const int64_t lim = tnodes ? half : real_k1;
+    for (int64_t base = 0; base < lim; base += NT) {
+      const int64_t i = base + tid;
+      uint32_t out[8];
+      const bool have = i < lim;
+      if (have) {
+        if (i < real_k1) {
+          uint32_t l[8], r[8];
+          load_digest_cg(src + (2 * i) * 32, l);
+          if (2 * i + 1 < real_k) {
+            load_digest_cg(src + (2 * i + 1) * 32, r);
+          } else {
+#pragma unroll
+            for (int w = 0; w < 8; ++w) r[w] = Z[8 * k + w];
+          }
+          hash_pair(l, r, out);
+        } else {
+#pragma unroll
+          for (int w = 0; w < 8; ++w) out[w] = Z[8 * (k + 1) + w];
+        }
+      }
+      __syncthreads();  // in-place mode: every read of this pass precedes the writes
+      if (have) store_digest(dst + i * 32, out);
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    uint32_t r[8];
+    load_digest_cg(tnodes ? tnodes + level_off(lp, lp) * 32 : tcroot, r);
+    store_digest(root_out, r);
+  }
+}
+
+// Common tail of a chunk CTA: reduce, publish, and finish the tree if last.
+template <int NT>
+__device__ __forceinline__ void chunk_tail(uint32_t (*sd)[NT], const TreeMeta& m, int layer,
+                                           int64_t chunk, const TreeOut& o) {
+  __shared__ int s_last;
+  const int tid = threadIdx.x;
+  const int lp = m.log2_pad, kc = m.log2_chunk;
+  uint8_t* tnodes = o.nodes ? o.nodes + (m.node_base + int64_t(layer) * m.node_stride) * 32 : nullptr;
+  uint8_t* tcroot = o.nodes ? nullptr : o.croots + (m.croot_base + int64_t(layer) * m.croot_stride) * 32;
+  const int tree = m.tree_base + layer;
+  chunk_reduce<NT>(sd, kc, tnodes, lp, chunk);
+  if (!tnodes && tid == 0) {
+    uint32_t r[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) r[w] = sd[w][0];
+    store_digest(tcroot + chunk * 32, r);
+  }
+  if (m.n_chunks == 1) {
+    finish_tree<NT>(tnodes, tcroot, m.n_leaves, lp, kc, 1, o.zero_roots, o.roots + int64_t(tree) * 32);
+    return;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(o.counters + tree, 1u);
+    s_last = (prev == unsigned(m.n_chunks - 1));
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    finish_tree<NT>(tnodes, tcroot, m.n_leaves, lp, kc, m.n_chunks, o.zero_roots,
+                    o.roots + int64_t(tree) * 32);
+    if (tid == 0) o.counters[tree] = 0u;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// f64 widening.  The message of hash_kv_entry holds f64le values
+// (merkle.rs:274-293); a K/V row of bf16 or f32 is widened exactly.
+// For an f64 d the two message words are bswap(lo32(d)), bswap(hi32(d)).
+// ---------------------------------------------------------------------------
+
+// Exact f32 -> f64 bit widening, every class: normal, zero, subnormal
+// (renormalised), infinity, NaN (payload kept, quiet bit set).
+__device__ __forceinline__ void f32_to_f64_bits(uint32_t f, uint32_t& hi, uint32_t& lo) {
+  const uint32_t s = f & 0x80000000u, a = f & 0x7FFFFFFFu;
+  const uint32_t e = a >> 23, m = a & 0x7FFFFFu;
+  if (e - 1u < 254u) {
+    hi = s | ((a >> 3) + 0x38000000u);
+    lo = m << 29;
+  } else if (a == 0) {
+    hi = s;
+    lo = 0;
+  } else if (e == 0) {
+    const int p = 31 - __clz(m);  // f32 subnormal m * 2^-149 = 2^(p-149) * 1.xxx
+    const uint64_t mant = (uint64_t(m) << (52 - p)) & 0xFFFFFFFFFFFFFull;
+    const uint64_t d = (uint64_t(p + 874) << 52) | mant;
+    hi = s | uint32_t(d >> 32);
+    lo = uint32_t(d);
+  } else {
+    hi = s | 0x7FF00000u | (m >> 3) | (m ? 0x80000u : 0u);
+    lo = m << 29;
+  }
+}
+
+// bf16 pair (two elements in one little-endian word) -> the big-endian
+// message word of hi32(f64) of each; lo32 is always 0 for a bf16 value.
+__device__ __forceinline__ void bf16x2_fast(uint32_t x, uint32_t& w0, uint32_t& w1) {
+  // Valid when both exponents are in [1, 254].
+  const uint32_t h0 = ((x & 0x8000u) << 16) | (((x << 13) & 0x0FFFE000u) + 0x38000000u);
+  const uint32_t h1 = (x & 0x80000000u) | (((x >> 3) & 0x0FFFE000u) + 0x38000000u);
+  w0 = bswap32(h0);
+  w1 = bswap32(h1);
+}
+
+__device__ __forceinline__ void bf16x2_exact(uint32_t x, uint32_t& w0, uint32_t& w1) {
+  uint32_t hi, lo;
+  f32_to_f64_bits(x << 16, hi, lo);
+  w0 = bswap32(hi);
+  f32_to_f64_bits(x & 0xFFFF0000u, hi, lo);
+  w1 = bswap32(hi);
+}
+
+// Nonzero when some bf16 of the pair has exponent 0 or 255 (zero,
+// subnormal, inf, NaN): SIMD test on the two 16-bit lanes.
+__device__ __forceinline__ uint32_t bf16x2_special(uint32_t x) {
+  const uint32_t y = x & 0x7F807F80u;
+  return ((y + 0x00800080u) | (y - 0x00800080u)) & 0x80008000u;
+}
+
+// Walks the 8-element chunks of a K/V row pair: K heads then V heads, each
+// head contiguous, heads stride_head apart.
+struct RowCursor {
+  const char* kb;
+  const char* vb;
+  int64_t hs;     // bytes between heads
+  int cb;         // bytes per chunk
+  int cph;        // chunks per head
+  int nh;
+  int sel, h, ci;
+  __device__ __forceinline__ const char* next() {
+    const char* p = (sel ? vb : kb) + int64_t(h) * hs + int64_t(ci) * cb;
+    if (++ci == cph) {
+      ci = 0;
+      if (++h == nh) {
+        h = 0;
+        sel = 1;
+      }
+    }
+    return p;
+  }
+};
+
+template <int DT> struct Chunk;
+template <> struct Chunk<0> {  // bf16: 8 elements = 16 bytes
+  uint4 q;
+  __device__ __forceinline__ void load(const char* p) { q = __ldg(reinterpret_cast<const uint4*>(p)); }
+};
+template <> struct Chunk<1> {  // f32: 32 bytes
+  uint4 q[2];
+  __device__ __forceinline__ void load(const char* p) {
+    q[0] = __ldg(reinterpret_cast<const uint4*>(p));
+    q[1] = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+  }
+};
+template <> struct Chunk<2> {  // f64: 64 bytes
+  uint4 q[4];
+  __device__ __forceinline__ void load(const char* p) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+  }
+};
+
+// Message words of element i (0..7) of a chunk: w[2j] = bswap(lo32),
+// w[2j+1] = bswap(hi32).  `out` receives elements [e0, e0+n).
+template <int DT, bool FAST>
+__device__ __forceinline__ void chunk_words(const Chunk<DT>& c, int e0, int n, uint32_t* out);
+
+template <>
+__device__ __forceinline__ void chunk_words<0, true>(const Chunk<0>& c, int e0, int n, uint32_t* out) {
+  const uint32_t x[4] = {c.q.x, c.q.y, c.q.z, c.q.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (2 * j + 1 < e0 || 2 * j >= e0 + n) continue;
+    uint32_t w0, w1;
+    bf16x2_fast(x[j], w0, w1);
+    if (2 * j >= e0) { out[2 * (2 * j - e0)] = 0; out[2 * (2 * j - e0) + 1] = w0; }
+    if (2 * j + 1 < e0 + n) { out[2 * (2 * j + 1 - e0)] = 0; out[2 * (2 * j + 1 - e0) + 1] = w1; }
+  }
+}
+template <>
+__device__ __forceinline__ void chunk_words<0, false>(const Chunk<0>& c, int e0, int n, uint32_t* out) {
+  const uint32_t x[4] = {c.q.x, c.q.y, c.q.z, c.q.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (2 * j + 1 < e0 || 2 * j >= e0 + n) continue;
+    uint32_t w0, w1;
+    bf16x2_exact(x[j], w0, w1);
+    if (2 * j >= e0) { out[2 * (2 * j - e0)] = 0; out[2 * (2 * j - e0) + 1] = w0; }
+    if (2 * j + 1 < e0 + n) { out[2 * (2 * j + 1 - e0)] = 0; out[2 * (2 * j + 1 - e0) + 1] = w1; }
+  }
+}
+template <bool FAST>
+__device__ __forceinline__ void f32_chunk_words(const Chunk<1>& c, int e0, int n, uint32_t* out) {
+  const uint32_t x[8] = {c.q[0].x, c.q[0].y, c.q[0].z, c.q[0].w, c.q[1].x, c.q[1].y, c.q[1].z, c.q[1].w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < e0 || i >= e0 + n) continue;
+    uint32_t hi, lo;
+    f32_to_f64_bits(x[i], hi, lo);
+    out[2 * (i - e0)] = bswap32(lo);
+    out[2 * (i - e0) + 1] = bswap32(hi);
+  }
+}
+template <>
+__device__ __forceinline__ void chunk_words<1, true>(const Chunk<1>& c, int e0, int n, uint32_t* out) {
+  f32_chunk_words<true>(c, e0, n, out);
+}
+template <>
+__device__ __forceinline__ void chunk_words<1, false>(const Chunk<1>& c, int e0, int n, uint32_t* out) {
+  f32_chunk_words<false>(c, e0, n, out);
+}
+template <bool FAST>
+__device__ __forceinline__ void f64_chunk_words(const Chunk<2>& c, int e0, int n, uint32_t* out) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < e0 || i >= e0 + n) continue;
+    const uint4& q = c.q[i >> 1];
+    const uint32_t lo = (i & 1) ? q.z : q.x;
+    const uint32_t hi = (i & 1) ? q.w : q.y;
+    out[2 * (i - e0)] = bswap32(lo);
+    out[2 * (i - e0) + 1] = bswap32(hi);
+  }
+}
+template <>
+__device__ __forceinline__ void chunk_words<2, true>(const Chunk<2>& c, int e0, int n, uint32_t* out) {
+  f64_chunk_words<true>(c, e0, n, out);
+}
+template <>
+__device__ __forceinline__ void chunk_words<2, false>(const Chunk<2>& c, int e0, int n, uint32_t* out) {
+  f64_chunk_words<false>(c, e0, n, out);
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t chunk_special(const Chunk<DT>& c);
+template <>
+__device__ __forceinline__ uint32_t chunk_special<0>(const Chunk<0>& c) {
+  return bf16x2_special(c.q.x) | bf16x2_special(c.q.y) | bf16x2_special(c.q.z) | bf16x2_special(c.q.w);
+}
+template <>
+__device__ __forceinline__ uint32_t chunk_special<1>(const Chunk<1>& c) { return 0; }
+template <>
+__device__ __forceinline__ uint32_t chunk_special<2>(const Chunk<2>& c) { return 0; }
+
+// One block = the last 2 elements of the previous chunk + the first 6 of
+// the current one (the 16-byte leaf prefix shifts f64 slots by two).
+template <int DT>
+__device__ __forceinline__ void block_words(const Chunk<DT>& prev, const Chunk<DT>& cur, uint32_t w[16]) {
+  if (chunk_special<DT>(prev) | chunk_special<DT>(cur)) {
+    chunk_words<DT, false>(prev, 6, 2, w);
+    chunk_words<DT, false>(cur, 0, 6, w + 4);
+  } else {
+    chunk_words<DT, true>(prev, 6, 2, w);
+    chunk_words<DT, true>(cur, 0, 6, w + 4);
+  }
+}
+
+// hash_kv_entry (merkle.rs:285-293) of one (layer, position) with
+// kv_dim % 8 == 0 and head_dim % 8 == 0.
+template <int DT>
+__device__ __forceinline__ void kv_leaf(uint32_t st[8], uint32_t layer, uint32_t pos, RowCursor rc,
+                                        int n_chunks, uint32_t bitlen) {
+  sha_init(st);
+  uint32_t w[16];
+  Chunk<DT> cur, nxt, prev;
+  cur.load(rc.next());
+  nxt.load(rc.next());
+  // Block 0: "vi-kv-v1" || u32le layer || u32le pos || elements 0..5.
+  w[0] = 0x76692d6bu;  // "vi-k"
+  w[1] = 0x762d7631u;  // "v-v1"
+  w[2] = bswap32(layer);
+  w[3] = bswap32(pos);
+  if (chunk_special<DT>(cur)) {
+    chunk_words<DT, false>(cur, 0, 6, w + 4);
+  } else {
+    chunk_words<DT, true>(cur, 0, 6, w + 4);
+  }
+  compress(st, w);
+  for (int b = 1; b < n_chunks; ++b) {
+    prev = cur;
+    cur = nxt;
+    if (b + 1 < n_chunks) nxt.load(rc.next());
+    block_words<DT>(prev, cur, w);
+    compress(st, w);
+  }
+  // Last block: elements 2*kv-2, 2*kv-1, then 0x80, zeros, bit length.
+  if (chunk_special<DT>(cur)) {
+    chunk_words<DT, false>(cur, 6, 2, w);
+  } else {
+    chunk_words<DT, true>(cur, 6, 2, w);
+  }
+  w[4] = 0x80000000u;
+#pragma unroll
+  for (int i = 5; i < 15; ++i) w[i] = 0;
+  w[15] = bitlen;
+  compress(st, w);
+}
+
+// Element offset of the row of position p, or -1 (error flagged) when the
+// row does not lie inside the cache buffer.
+__device__ __forceinline__ int64_t kv_row(const KvArgs& a, const TreeMeta& m, int64_t p) {
+  int64_t off;
+  if (a.paged) {
+    const int32_t page = __ldg(a.block_tables + int64_t(m.seq) * a.max_blocks + p / a.block_size);
+    off = int64_t(page) * a.stride_page + (p % a.block_size) * a.stride_row;
+    if (page < 0) off = -1;
+  } else {
+    off = (m.src_off + p) * a.stride_row;
+  }
+  if (off < 0 || off + a.row_span > a.cache_elems) {
+    atomicExch(a.err, 1);
+    return -1;
+  }
+  return off;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kTreeThreads) kv_commit_kernel(KvArgs a) {
+  __shared__ uint32_t sd[8][kTreeThreads];
+  const int2 it = a.items[blockIdx.x];
+  const TreeMeta m = a.meta[it.x];
+  const int layer = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int c = 1 << m.log2_chunk;
+  const int64_t chunk = it.y;
+  const int64_t p = chunk * c + tid;
+  if (tid < c) {
+    uint32_t d[8];
+    const int64_t row = p < m.n_leaves ? kv_row(a, m, p) : -1;
+    if (row >= 0) {
+      constexpr int esz = DT == 0 ? 2 : (DT == 1 ? 4 : 8);
+      const int64_t off = row * esz;
+      RowCursor rc;
+      rc.kb = static_cast<const char*>(a.k_layers[layer]) + off;
+      rc.vb = static_cast<const char*>(a.v_layers[layer]) + off;
+      rc.hs = a.stride_head * esz;
+      rc.cb = 8 * esz;
+      rc.cph = a.head_dim >> 3;
+      rc.nh = a.n_heads;
+      rc.sel = 0; rc.h = 0; rc.ci = 0;
+      const int kv = a.n_heads * a.head_dim;
+      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(p), rc, kv >> 2, uint32_t(16 + 16 * kv) * 8u);
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = 0;
+    }
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sd[w][tid] = d[w];
+    if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + int64_t(layer) * m.node_stride + p) * 32, d);
+  }
+  __syncthreads();
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+}
+
+// Generic path for any kv_dim / head_dim: the stream engine, element by element.
+template <int DT>
+__global__ void __launch_bounds__(kTreeThreads) kv_commit_generic_kernel(KvArgs a) {
+  __shared__ uint32_t sd[8][kTreeThreads];
+  __shared__ uint32_t sbuf[16 * kTreeThreads];
+  const int2 it = a.items[blockIdx.x];
+  const TreeMeta m = a.meta[it.x];
+  const int layer = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int c = 1 << m.log2_chunk;
+  const int64_t chunk = it.y;
+  const int64_t p = chunk * c + tid;
+  if (tid < c) {
+    uint32_t d[8];
+    const int64_t row = p < m.n_leaves ? kv_row(a, m, p) : -1;
+    if (row >= 0) {
+      constexpr int esz = DT == 0 ? 2 : (DT == 1 ? 4 : 8);
+      const int64_t off = row * esz;
+      Sha256Stream<kTreeThreads> s;
+      s.init(sbuf + tid);
+      s.put_be(0x76692d6bu);
+      s.put_be(0x762d7631u);
+      s.put_be(bswap32(uint32_t(a.layer_base + layer)));
+      s.put_be(bswap32(uint32_t(p)));
+      for (int sel = 0; sel < 2; ++sel) {
+        const char* row = static_cast<const char*>(sel ? a.v_layers[layer] : a.k_layers[layer]) + off;
+        for (int h = 0; h < a.n_heads; ++h) {
+          const char* hp = row + int64_t(h) * a.stride_head * esz;
+          for (int i = 0; i < a.head_dim; ++i) {
+            uint32_t hi, lo;
+            if (DT == 0) {
+              f32_to_f64_bits(uint32_t(__ldg(reinterpret_cast<const uint16_t*>(hp) + i)) << 16, hi, lo);
+            } else if (DT == 1) {
+              f32_to_f64_bits(__ldg(reinterpret_cast<const uint32_t*>(hp) + i), hi, lo);
+            } else {
+              const uint2 v = __ldg(reinterpret_cast<const uint2*>(hp) + i);
+              lo = v.x;
+              hi = v.y;
+            }
+            s.put_be(bswap32(lo));
+            s.put_be(bswap32(hi));
+          }
+        }
+      }
+      s.finish();
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = s.h[w];
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = 0;
+    }
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sd[w][tid] = d[w];
+    if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + int64_t(layer) * m.node_stride + p) * 32, d);
+  }
+  __syncthreads();
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+}
+
+__global__ void __launch_bounds__(kTreeThreads) tree_commit_kernel(TreeArgs a) {
+  __shared__ uint32_t sd[8][kTreeThreads];
+  const int2 it = a.items[blockIdx.x];
+  const TreeMeta m = a.meta[it.x];
+  const int tid = threadIdx.x;
+  const int c = 1 << m.log2_chunk;
+  const int64_t chunk = it.y;
+  const int64_t p = chunk * c + tid;
+  if (tid < c) {
+    uint32_t d[8];
+    if (p < m.n_leaves) {
+      load_digest(a.leaves + (m.src_off + p) * 32, d);
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = 0;
+    }
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sd[w][tid] = d[w];
+    if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + p) * 32, d);
+  }
+  __syncthreads();
+  chunk_tail<kTreeThreads>(sd, m, 0, chunk, a.out);
+}
+
+__global__ void zero_roots_kernel(uint32_t* z) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  uint32_t cur[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int k = 0; k <= kMaxTreeHeight; ++k) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) z[8 * k + w] = cur[w];
+    uint32_t nxt[8];
+    hash_pair(cur, cur, nxt);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) cur[w] = nxt[w];
+  }
+}
+
+// merkle::prove (merkle.rs:79-99): one thread per (opening, level).
+__global__ void prove_kernel(const uint8_t* nodes, const ProveReq* reqs, int n, int max_depth,
+                             uint8_t* siblings) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gid >= int64_t(n) * max_depth) return;
+  const int r = int(gid / max_depth);
+  const int k = int(gid % max_depth);
+  const ProveReq q = reqs[r];
+  if (k >= q.log2_pad) return;
+  const int64_t sib = int64_t((q.leaf >> k) ^ 1u);
+  const uint4* src = reinterpret_cast<const uint4*>(nodes + (q.node_base + level_off(q.log2_pad, k) + sib) * 32);
+  uint4* dst = reinterpret_cast<uint4*>(siblings + gid * 32);
+  dst[0] = src[0];
+  dst[1] = src[1];
+}
+
+cudaError_t launch_zero_roots(uint32_t* z, cudaStream_t s) {
+  zero_roots_kernel<<<1, 32, 0, s>>>(z);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kv_commit(const KvArgs& a, int n_items, int n_layers, int dtype, bool fast,
+                             cudaStream_t s) {
+  dim3 grid(n_items, n_layers);
+  if (fast) {
+    switch (dtype) {
+      case 0: kv_commit_kernel<0><<<grid, kTreeThreads, 0, s>>>(a); break;
+      case 1: kv_commit_kernel<1><<<grid, kTreeThreads, 0, s>>>(a); break;
+      default: kv_commit_kernel<2><<<grid, kTreeThreads, 0, s>>>(a); break;
+    }
+  } else {
+    switch (dtype) {
+      case 0: kv_commit_generic_kernel<0><<<grid, kTreeThreads, 0, s>>>(a); break;
+      case 1: kv_commit_generic_kernel<1><<<grid, kTreeThreads, 0, s>>>(a); break;
+      default: kv_commit_generic_kernel<2><<<grid, kTreeThreads, 0, s>>>(a); break;
+    }
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tree_commit(const TreeArgs& a, int n_items, cudaStream_t s) {
+  tree_commit_kernel<<<n_items, kTreeThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prove(const uint8_t* nodes, const ProveReq* reqs, int n, int max_depth,
+                         uint8_t* siblings, cudaStream_t s) {
+  const int64_t total = int64_t(n) * max_depth;
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  prove_kernel<<<int((total + threads - 1) / threads), threads, 0, s>>>(nodes, reqs, n, max_depth, siblings);
+  return cudaGetLastError();
+}
+
+}  // namespace vc

@@ -1,0 +1,173 @@
+// Per-thread streaming SHA-256 for messages built from fields at arbitrary
+// byte offsets (the retained-state leaf of merkle.rs:144-161 has 4101-byte
+// layer records, so its a_i8 rows start at every alignment mod 4).
+//
+// The 16-word block buffer lives in shared memory, word-major across the CTA
+// (word k of thread tid at buf[k * NT]), so every access of a warp is one
+// conflict-free wavefront.  All threads of a warp hash messages of the same
+// layout, so the fill position -- and every branch on it -- is warp-uniform.
+#pragma once
+#include "sha256_core.cuh"
+
+namespace vc {
+
+template <int NT>
+struct Sha256Stream {
+  uint32_t h[8];
+  uint32_t* buf;    // this thread's column of the CTA's [16][NT] buffer
+  uint32_t fill;    // bytes of the current block, pending partial word included (0..63)
+  uint32_t carry;   // the fill % 4 pending bytes, left-aligned big-endian
+  uint64_t total;   // message bytes appended
+
+  __device__ __forceinline__ void init(uint32_t* column) {
+    sha_init(h);
+    buf = column;
+    fill = 0;
+    carry = 0;
+    total = 0;
+  }
+
+  __device__ __forceinline__ void block() {
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) w[k] = buf[k * NT];
+    compress(h, w);
+  }
+
+  // Append 4 bytes given as a big-endian word.
+  __device__ __forceinline__ void put_be(uint32_t wbe) {
+    const uint32_t r = fill & 3u;
+    const uint32_t k = fill >> 2;
+    if (r == 0) {
+      buf[k * NT] = wbe;
+    } else {
+      buf[k * NT] = carry | (wbe >> (8u * r));
+      carry = wbe << (32u - 8u * r);
+    }
+    fill += 4;
+    total += 4;
+    if (fill >= 64) {
+      block();
+      fill -= 64;
+    }
+  }
+
+  // Append 4 bytes in memory order (a little-endian 32-bit load).
+  __device__ __forceinline__ void put_le(uint32_t x) { put_be(bswap32(x)); }
+
+  // Append n (1..3) bytes, left-aligned in v (big-endian), low bytes zero.
+  __device__ __forceinline__ void put_small(uint32_t v, uint32_t n) {
+    const uint32_t r = fill & 3u;
+    if (r + n < 4) {
+      carry |= v >> (8u * r);
+    } else {
+      buf[(fill >> 2) * NT] = carry | (v >> (8u * r));
+      carry = v << (8u * (4u - r));   // r >= 1 here, so the shift is < 32
+    }
+    fill += n;
+    total += n;
+    if (fill >= 64) {
+      block();
+      fill -= 64;
+    }
+  }
+
+  __device__ __forceinline__ void put_byte(uint32_t b) { put_small(b << 24, 1); }
+
+  // Append the 8 words of a digest (32 bytes).
+  __device__ __forceinline__ void put_digest(const uint32_t d[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) put_be(d[i]);
+  }
+
+  // Append len bytes from p (any alignment).
+  __device__ __forceinline__ void put_array(const uint8_t* p, int64_t len) {
+    while (len > 0 && (reinterpret_cast<uintptr_t>(p) & 3u) != 0) {
+      put_byte(__ldg(p));
+      ++p;
+      --len;
+    }
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+    int64_t nw = len >> 2;
+    // Reach 16-byte alignment with single words.
+    while (nw > 0 && (reinterpret_cast<uintptr_t>(q) & 15u) != 0) {
+      put_le(__ldg(q));
+      ++q;
+      --nw;
+    }
+    const uint4* v = reinterpret_cast<const uint4*>(q);
+    int64_t nv = nw >> 2;
+    uint4 nxt = make_uint4(0, 0, 0, 0);
+    if (nv > 0) nxt = __ldg(v);
+    for (int64_t i = 0; i < nv; ++i) {
+      const uint4 cur = nxt;
+      if (i + 1 < nv) nxt = __ldg(v + i + 1);
+      if (fill + 16 < 64) {
+        // The 16 bytes stay inside the current block.
+        const uint32_t r = fill & 3u;
+        const uint32_t k = fill >> 2;
+        const uint32_t a = bswap32(cur.x), b = bswap32(cur.y), c = bswap32(cur.z), d = bswap32(cur.w);
+        if (r == 0) {
+          buf[(k + 0) * NT] = a;
+          buf[(k + 1) * NT] = b;
+          buf[(k + 2) * NT] = c;
+          buf[(k + 3) * NT] = d;
+        } else {
+          const uint32_t sr = 8u * r, sl = 32u - 8u * r;
+          buf[(k + 0) * NT] = carry | (a >> sr);
+          buf[(k + 1) * NT] = (a << sl) | (b >> sr);
+          buf[(k + 2) * NT] = (b << sl) | (c >> sr);
+          buf[(k + 3) * NT] = (c << sl) | (d >> sr);
+          carry = d << sl;
+        }
+        fill += 16;
+        total += 16;
+      } else {
+        put_le(cur.x);
+        put_le(cur.y);
+        put_le(cur.z);
+        put_le(cur.w);
+      }
+    }
+    q += nv << 2;
+    for (int64_t i = 0; i < (nw & 3); ++i) put_le(__ldg(q + i));
+    q += nw & 3;
+    const uint32_t tail = static_cast<uint32_t>(len & 3);
+    if (tail) {
+      // Read the last bytes one at a time: the word holding them may end
+      // past the caller's buffer.
+      const uint8_t* t = reinterpret_cast<const uint8_t*>(q);
+      uint32_t v = 0;
+      for (uint32_t i = 0; i < tail; ++i) v |= static_cast<uint32_t>(__ldg(t + i)) << (24 - 8 * i);
+      put_small(v, tail);
+    }
+  }
+
+  // FIPS 180-4 padding and length; the digest lands in h.
+  __device__ __forceinline__ void finish() {
+    const uint64_t bits = total * 8ull;
+    put_byte(0x80);
+    if (fill & 3u) {
+      buf[(fill >> 2) * NT] = carry;
+      fill = (fill + 3u) & ~3u;
+      carry = 0;
+    }
+    if (fill > 56) {
+      for (uint32_t k = fill >> 2; k < 16; ++k) buf[k * NT] = 0;
+      block();
+      fill = 0;
+    }
+    for (uint32_t k = fill >> 2; k < 14; ++k) buf[k * NT] = 0;
+    buf[14 * NT] = static_cast<uint32_t>(bits >> 32);
+    buf[15 * NT] = static_cast<uint32_t>(bits);
+    block();
+    fill = 0;
+  }
+
+  // Append an ASCII tag (domain separator) byte by byte.
+  __device__ __forceinline__ void put_tag(const char* s, int n) {
+    for (int i = 0; i < n; ++i) put_byte(static_cast<uint8_t>(s[i]));
+  }
+};
+
+}  // namespace vc

@@ -1,0 +1,168 @@
+// Retained-state ("trace") leaves, the IO hash chain, and small tagged hashes.
+#include "sha256_core.cuh"
+#include "sha256_stream.cuh"
+#include "vc_internal.h"
+
+namespace vc {
+
+constexpr int kTraceThreads = 128;
+
+// Domain separators (ASCII), merkle.rs:147, 179, 206, 233, 251, 555, 563, 574.
+__device__ const char kTagRetained[] = "vi-retained-v3";
+__device__ const char kTagFr[] = "vi-retained-fr-v1";
+__device__ const char kTagLp[] = "vi-retained-lp-v1";
+__device__ const char kTagLogits[] = "vi-retained-logits-v1";
+__device__ const char kTagPrompt[] = "vi-prompt-v1";
+__device__ const char kTagSeed[] = "vi-seed-v1";
+
+// One thread per token: hash_retained_state_direct (merkle.rs:144-161), then
+// the optional wraps of hash_retained_with_captured_logits (merkle.rs:170-241).
+__global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(TraceArgs a) {
+  __shared__ uint32_t sbuf[16 * kTraceThreads];
+  const int t = blockIdx.x * kTraceThreads + threadIdx.x;
+  if (t >= a.n_tokens) return;
+  const int32_t* tk = a.tok + 5 * int64_t(t);
+  const int f = tk[0];
+  const int64_t row = tk[1];
+  Sha256Stream<kTraceThreads> s;
+  s.init(sbuf + threadIdx.x);
+  s.put_tag(kTagRetained, 14);
+  for (int l = 0; l < a.n_layers; ++l) {
+    const int64_t fl = int64_t(f) * a.n_layers + l;
+    const uint8_t* arow = static_cast<const uint8_t*>(a.a_rows[fl]) + row * a.hidden;
+    s.put_array(arow, a.hidden);
+    s.put_le(__ldg(static_cast<const uint32_t*>(a.scale_a[fl]) + row * a.scale_stride));
+    if (a.x_rows) {
+      s.put_byte(1);
+      const uint8_t* xrow = static_cast<const uint8_t*>(a.x_rows[fl]) + row * a.hidden;
+      s.put_array(xrow, a.hidden);
+      s.put_le(__ldg(static_cast<const uint32_t*>(a.scale_x[fl]) + row * a.scale_x_stride));
+    } else {
+      s.put_byte(0);
+    }
+  }
+  s.finish();
+  uint32_t d[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) d[w] = s.h[w];
+  if (tk[2] >= 0) {
+    s.init(sbuf + threadIdx.x);
+    s.put_tag(kTagFr, 17);
+    s.put_digest(d);
+    s.put_array(a.fr + int64_t(tk[2]) * a.fr_stride * 4, int64_t(a.fr_dim) * 4);
+    s.finish();
+#pragma unroll
+    for (int w = 0; w < 8; ++w) d[w] = s.h[w];
+  }
+  if (tk[3] >= 0) {
+    s.init(sbuf + threadIdx.x);
+    s.put_tag(kTagLp, 17);
+    s.put_digest(d);
+    s.put_array(a.lp + int64_t(tk[3]) * a.lp_stride * 2, int64_t(a.lp_dim) * 2);
+    s.finish();
+#pragma unroll
+    for (int w = 0; w < 8; ++w) d[w] = s.h[w];
+  }
+  if (tk[4] >= 0) {
+    s.init(sbuf + threadIdx.x);
+    s.put_tag(kTagLogits, 21);
+    s.put_digest(d);
+    s.put_array(a.logits + int64_t(tk[4]) * a.logits_stride * 4, int64_t(a.vocab) * 4);
+    s.finish();
+#pragma unroll
+    for (int w = 0; w < 8; ++w) d[w] = s.h[w];
+  }
+  store_digest(a.leaves + int64_t(t) * 32, d);
+}
+
+// IO chain of one sequence per thread (prover/src/lib.rs:403-410):
+//   prev = io_genesis_v4(prompt_hash)  = SHA256("vi-io-genesis-v4" || ph)
+//   io_t = io_hash_v4(leaf_t, tok_t, prev) = SHA256("vi-io-v4" || leaf || u32le tok || prev)
+// The 76-byte message is two blocks: [tag(2) leaf(8) tok(1) prev0..4] and
+// [prev5..7, 0x80000000, 0 x 11, 608].
+__global__ void io_chain_kernel(int n_seqs, const int64_t* tok_off, const uint8_t* leaves,
+                                const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n_seqs) return;
+  uint32_t prev[8];
+  {
+    uint32_t ph[8];
+    load_digest(prompt_hash + int64_t(s) * 32, ph);
+    uint32_t w[16] = {0x76692d69u, 0x6f2d6765u, 0x6e657369u, 0x732d7634u,  // "vi-io-genesis-v4"
+                      ph[0], ph[1], ph[2], ph[3], ph[4], ph[5], ph[6], ph[7],
+                      0x80000000u, 0u, 0u, 384u};
+    sha_init(prev);
+    compress(prev, w);
+  }
+  const int64_t t0 = tok_off[s], t1 = tok_off[s + 1];
+  if (t0 >= t1) return;
+  uint32_t leaf[8], tok;
+  load_digest(leaves + t0 * 32, leaf);
+  tok = token_ids[t0];
+  for (int64_t t = t0; t < t1; ++t) {
+    // Next token's inputs do not depend on the chain: fetch them now.
+    uint32_t nleaf[8], ntok = 0;
+    if (t + 1 < t1) {
+      load_digest(leaves + (t + 1) * 32, nleaf);
+      ntok = token_ids[t + 1];
+    }
+    uint32_t w[16] = {0x76692d69u, 0x6f2d7634u,  // "vi-io-v4"
+                      leaf[0], leaf[1], leaf[2], leaf[3], leaf[4], leaf[5], leaf[6], leaf[7],
+                      bswap32(tok), prev[0], prev[1], prev[2], prev[3], prev[4]};
+    uint32_t st[8];
+    sha_init(st);
+    compress(st, w);
+    uint32_t w2[16] = {prev[5], prev[6], prev[7], 0x80000000u, 0u, 0u, 0u, 0u,
+                       0u, 0u, 0u, 0u, 0u, 0u, 0u, 608u};
+    compress(st, w2);
+    store_digest(io + t * 32, st);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { prev[i] = st[i]; leaf[i] = nleaf[i]; }
+    tok = ntok;
+  }
+}
+
+// SHA256(tag || data_i), one thread per message.  tag 0: "vi-prompt-v1"
+// over [off[i], off[i+1]) (hash_prompt, merkle.rs:561-566); tag 1:
+// "vi-seed-v1" over 32 bytes at data + 32 i (hash_seed, merkle.rs:553-558).
+__global__ void __launch_bounds__(kTraceThreads) tagged_hash_kernel(int n, int tag, const uint8_t* data,
+                                                                     const int64_t* off, int64_t fixed_len,
+                                                                     uint8_t* out) {
+  __shared__ uint32_t sbuf[16 * kTraceThreads];
+  const int i = blockIdx.x * kTraceThreads + threadIdx.x;
+  if (i >= n) return;
+  const int64_t b = off ? off[i] : int64_t(i) * fixed_len;
+  const int64_t len = off ? off[i + 1] - off[i] : fixed_len;
+  Sha256Stream<kTraceThreads> s;
+  s.init(sbuf + threadIdx.x);
+  if (tag == 0) s.put_tag(kTagPrompt, 12); else s.put_tag(kTagSeed, 10);
+  if (len > 0) s.put_array(data + b, len);
+  s.finish();
+  store_digest(out + int64_t(i) * 32, s.h);
+}
+
+cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s) {
+  if (a.n_tokens == 0) return cudaSuccess;
+  trace_leaf_kernel<<<(a.n_tokens + kTraceThreads - 1) / kTraceThreads, kTraceThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
+                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io,
+                            cudaStream_t s) {
+  // One thread per sequence; spread sequences over SMs (32 per CTA).
+  const int threads = 32;
+  io_chain_kernel<<<(n_seqs + threads - 1) / threads, threads, 0, s>>>(n_seqs, tok_off_dev, leaves, token_ids,
+                                                                      prompt_hash, io);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tagged_hash(int n, int tag, const uint8_t* data, const int64_t* off_dev,
+                               int64_t fixed_len, uint8_t* out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  tagged_hash_kernel<<<(n + kTraceThreads - 1) / kTraceThreads, kTraceThreads, 0, s>>>(n, tag, data, off_dev,
+                                                                                   fixed_len, out);
+  return cudaGetLastError();
+}
+
+}  // namespace vc

@@ -1,0 +1,99 @@
+// Internal declarations shared by the CUDA translation units of libvcommit.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vc {
+
+constexpr int kTreeThreads = 128;  // leaves per CTA of the Merkle kernels (chunk cap)
+constexpr int kLog2TreeThreads = 7;
+constexpr int kMaxTreeHeight = 62; // zero-subtree table size - 1
+
+// One leaf group: a tree (generic) or all n_layers trees of one sequence (KV).
+struct TreeMeta {
+  int64_t n_leaves;
+  int64_t node_base;     // index (in 32-byte nodes) of layer 0's tree
+  int64_t node_stride;   // nodes between consecutive layers' trees
+  int64_t croot_base;    // roots-only mode: chunk-root slot of layer 0
+  int64_t croot_stride;  // roots-only mode: slots between layers
+  int64_t src_off;       // KV contiguous layout: row of position 0; generic: first leaf
+  int32_t log2_pad;
+  int32_t log2_chunk;
+  int32_t n_chunks;      // chunks holding at least one real leaf
+  int32_t tree_base;     // tree index of layer 0 (tree = tree_base + layer)
+  int32_t seq;           // KV: block-table row
+  int32_t pad_;
+};
+
+struct TreeOut {
+  uint8_t* nodes;            // full node arrays, or nullptr (roots only)
+  uint8_t* croots;           // chunk-root scratch, used when nodes == nullptr
+  uint32_t* counters;        // [n_trees] finished-chunk counters, zero on entry and on exit
+  uint8_t* roots;            // [n_trees][32]
+  const uint32_t* zero_roots;// [kMaxTreeHeight + 1][8] Z_k words
+};
+
+struct KvArgs {
+  const TreeMeta* meta;
+  const int2* items;         // (meta index, chunk index) per CTA column
+  const void* const* k_layers;
+  const void* const* v_layers;
+  const int32_t* block_tables;
+  int64_t stride_page, stride_row, stride_head;  // elements
+  int32_t block_size, max_blocks;
+  int32_t n_heads, head_dim;
+  int32_t layer_base;
+  int32_t paged;
+  int64_t cache_elems;       // every row must lie inside [0, cache_elems) elements
+  int64_t row_span;          // (n_heads - 1) * stride_head + head_dim: extent of one row
+  int* err;                  // set to 1 when a row falls outside the cache
+  TreeOut out;
+};
+
+struct TreeArgs {
+  const TreeMeta* meta;
+  const int2* items;
+  const uint8_t* leaves;
+  TreeOut out;
+};
+
+struct ProveReq {
+  int64_t node_base;   // first node of the tree
+  uint32_t leaf;
+  int32_t log2_pad;
+};
+
+cudaError_t launch_zero_roots(uint32_t* z, cudaStream_t s);
+cudaError_t launch_kv_commit(const KvArgs& a, int n_items, int n_layers, int dtype, bool fast,
+                             cudaStream_t s);
+cudaError_t launch_tree_commit(const TreeArgs& a, int n_items, cudaStream_t s);
+cudaError_t launch_prove(const uint8_t* nodes, const ProveReq* reqs, int n, int max_depth,
+                         uint8_t* siblings, cudaStream_t s);
+
+// trace.cu
+struct TraceArgs {
+  int32_t n_tokens, n_layers, hidden;
+  const int32_t* tok;           // [n_tokens][5]: fwd, row, fr_row, lp_row, logits_row
+  const void* const* a_rows;    // [n_fwd * n_layers]
+  const void* const* scale_a;
+  int64_t scale_stride;
+  const void* const* x_rows;    // or nullptr
+  const void* const* scale_x;
+  int64_t scale_x_stride;
+  const uint8_t* fr; int32_t fr_dim; int64_t fr_stride;
+  const uint8_t* lp; int32_t lp_dim; int64_t lp_stride;
+  const uint8_t* logits; int32_t vocab; int64_t logits_stride;
+  uint8_t* leaves;
+};
+cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s);
+cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
+                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io,
+                            cudaStream_t s);
+cudaError_t launch_tagged_hash(int n, int tag, const uint8_t* data, const int64_t* off_dev,
+                               int64_t fixed_len, uint8_t* out, cudaStream_t s);
+
+// int_peak.cu
+cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,
+                            double* ops_per_launch);
+
+}  // namespace vc

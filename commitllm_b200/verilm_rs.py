@@ -1,0 +1,345 @@
+"""Drop-in for the commit half of the reference's ``verilm_rs`` PyO3 module.
+
+Same entry points, argument meanings and errors as
+``crates/verilm-py/src/lib.rs``:
+
+* :func:`commit_minimal_from_captures` (lib.rs:800-985)
+* :func:`commit_minimal_packed` (lib.rs:1189-1310)
+* handles with ``commitment_json``, ``merkle_root_hex``, ``io_root_hex``,
+  ``manifest_hash_hex``, ``n_tokens``, ``kv_roots_hex`` (lib.rs:651-674).
+
+The hashing runs on the GPU through libvcommit; inputs may be host buffers
+(copied once to the device) or CUDA tensors (read in place).  KV roots come
+from the device KV cache (``kv_cache=``), committing the same leaf encoding
+``hash_kv_entry`` (merkle.rs:285-293) over the cache's values widened to f64.
+
+Not provided here (outside the commitment hot path): the deployment-manifest
+hash (``manifest=`` raises NotImplementedError), ``compute_kv_transcript``
+from captured x_attn and weights (``weight_provider=`` is accepted for
+signature compatibility but unused), and ``audit_v4``'s shell opening.
+Openings of the committed trees are available as ``*_proof`` methods.
+"""
+from __future__ import annotations
+
+import json
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import commit as C
+
+
+def _f32_host(x) -> np.ndarray:
+    if isinstance(x, torch.Tensor):
+        x = x.detach().cpu().numpy()
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32).ravel())
+
+
+def _u8_host(x) -> np.ndarray:
+    if isinstance(x, (bytes, bytearray, memoryview)):
+        return np.frombuffer(bytes(x), dtype=np.uint8)
+    if isinstance(x, torch.Tensor):
+        x = x.detach().cpu().contiguous().view(torch.uint8).numpy() if x.dtype != torch.uint8 else x.detach().cpu().numpy()
+    return np.ascontiguousarray(np.asarray(x).view(np.uint8).ravel())
+
+
+def _rows_tensor(ctx: C.Context, items, dtype_np, dtype_t, name: str):
+    """Stack a per-token list into a device [rows, dim] tensor (uniform dim)."""
+    if isinstance(items, torch.Tensor) and items.is_cuda:
+        t = items if items.dim() == 2 else items.reshape(items.shape[0], -1)
+        return t.contiguous(), t.shape[0]
+    arrs = []
+    for it in items:
+        if isinstance(it, torch.Tensor):
+            it = it.detach().cpu().contiguous().numpy()
+        arrs.append(np.ascontiguousarray(np.asarray(it).view(dtype_np).ravel()))
+    if not arrs:
+        return None, 0
+    dims = {a.size for a in arrs}
+    if len(dims) != 1:
+        raise ValueError(f"{name}: every token's row must have the same length")
+    host = np.stack(arrs)
+    return ctx.to_device(host), host.shape[0]
+
+
+class _Committed:
+    """Device results of one request's commit; host copies made on first use."""
+
+    def __init__(self, ctx, n_tokens, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees,
+                 n_kv_layers):
+        self._ctx = ctx
+        self._n_tokens = n_tokens
+        self._token_ids = list(token_ids)
+        self._n_prompt_tokens = n_prompt_tokens
+        self._digests = digests          # device [4 + ..., 32]: trace root, io root, prompt hash, seed commitment
+        self._trees = trees              # TreeSet: tree 0 trace, tree 1 io
+        self._kv_roots = kv_roots        # device [n_layers, 32] or None
+        self._kv_trees = kv_trees
+        self._n_kv_layers = n_kv_layers
+        self._host = None
+
+    def _h(self):
+        if self._host is None:
+            self._ctx.sync()
+            d = self._digests.cpu().numpy()
+            kv = self._kv_roots.cpu().numpy() if self._kv_roots is not None else np.zeros((0, 32), np.uint8)
+            self._host = {"merkle_root": bytes(d[0]), "io_root": bytes(d[1]), "prompt_hash": bytes(d[2]),
+                          "seed_commitment": bytes(d[3]), "kv_roots": [bytes(r) for r in kv]}
+        return self._host
+
+    # --- reference handle API (verilm-py/src/lib.rs:651-674) ---
+    def commitment(self) -> dict:
+        h = self._h()
+        return {
+            "merkle_root": list(h["merkle_root"]), "io_root": list(h["io_root"]), "n_tokens": self._n_tokens,
+            "manifest_hash": None, "input_spec_hash": None, "model_spec_hash": None,
+            "decode_spec_hash": None, "output_spec_hash": None, "version": "V4",
+            "prompt_hash": list(h["prompt_hash"]), "seed_commitment": list(h["seed_commitment"]),
+            "n_prompt_tokens": self._n_prompt_tokens, "kv_roots": [list(r) for r in h["kv_roots"]],
+        }
+
+    def commitment_json(self) -> str:
+        """serde_json form of ``BatchCommitment`` (types.rs:1710-1759)."""
+        return json.dumps(self.commitment(), separators=(",", ":"))
+
+    def merkle_root_hex(self) -> str:
+        return self._h()["merkle_root"].hex()
+
+    def io_root_hex(self) -> str:
+        return self._h()["io_root"].hex()
+
+    def manifest_hash_hex(self):
+        return None
+
+    def n_tokens(self) -> int:
+        return self._n_tokens
+
+    def kv_roots_hex(self) -> List[str]:
+        return [r.hex() for r in self._h()["kv_roots"]]
+
+    # --- openings (merkle::prove over the committed trees) ---
+    def _proof(self, trees: C.TreeSet, tree: int, index: int):
+        sib, depth = trees.prove([tree], [index])
+        s = sib[0, :depth[0]].cpu().numpy()
+        return {"leaf_index": int(index), "siblings": [bytes(x).hex() for x in s]}
+
+    def retained_proof(self, token_index: int) -> dict:
+        """MerkleProof of the token's retained leaf against merkle_root."""
+        if not 0 <= token_index < self._n_tokens:
+            raise ValueError(f"token_index {token_index} out of range (n_tokens={self._n_tokens})")
+        return self._proof(self._trees, 0, token_index)
+
+    def io_proof(self, token_index: int) -> dict:
+        """MerkleProof of the token's IO chain value against io_root."""
+        if not 0 <= token_index < self._n_tokens:
+            raise ValueError(f"token_index {token_index} out of range (n_tokens={self._n_tokens})")
+        return self._proof(self._trees, 1, token_index)
+
+    def kv_proof(self, layer: int, position: int) -> dict:
+        """MerkleProof of KV leaf (layer, position) against kv_roots[layer]."""
+        if self._kv_trees is None:
+            raise ValueError("no KV transcript was committed")
+        if not 0 <= layer < self._n_kv_layers:
+            raise ValueError(f"layer {layer} out of range")
+        return self._proof(self._kv_trees, layer, position)
+
+    def leaf_hashes(self) -> torch.Tensor:
+        """The retained leaves (tree 0's level 0), a device view ``[n_tokens, 32]``."""
+        return self._trees.nodes(0)[: self._n_tokens]
+
+    def io_hashes(self) -> torch.Tensor:
+        return self._trees.nodes(1)[: self._n_tokens]
+
+
+class MinimalBatchStateHandle(_Committed):
+    """Counterpart of ``MinimalBatchStateHandle`` (verilm-py/src/lib.rs:576-787)."""
+
+    def __init__(self, *a, x_attn=None, **k):
+        super().__init__(*a, **k)
+        self._x_attn = x_attn
+
+    def has_captured_x_attn(self) -> bool:
+        return self._x_attn is not None
+
+    def clear_captured_x_attn(self) -> None:
+        self._x_attn = None
+
+
+class PackedBatchStateHandle(_Committed):
+    """Counterpart of ``PackedBatchStateHandle`` (verilm-py/src/lib.rs:993-1168)."""
+
+
+def _check_common(token_ids, sampling_seed, manifest):
+    if manifest is not None:
+        raise NotImplementedError("manifest hashing is not part of the GPU commit path; pass manifest=None")
+    seed = bytes(sampling_seed)
+    if len(seed) != 32:
+        raise ValueError("sampling_seed must be exactly 32 bytes")
+    for t in token_ids:
+        if not 0 <= int(t) <= 0xFFFFFFFF:
+            raise ValueError(f"token id {t} does not fit u32")
+    return seed
+
+
+def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens, kv_cache, handle_cls, **extra):
+    n = len(layout.tok_fwd)
+    if n != len(token_ids):
+        raise ValueError("retained state count must match token_ids")
+    if n == 0:
+        raise ValueError("need at least one leaf")
+    # leaves and io values in one buffer so both trees build in one launch
+    both = ctx.empty(2 * n, 32)
+    C.trace_leaves(ctx, layout, out=both[:n])
+    tok = ctx.to_device(np.asarray([int(t) for t in token_ids], dtype=np.uint32).view(np.int32))
+    digests = ctx.empty(4, 32)
+    ph = C.prompt_hashes(ctx, [bytes(prompt)])
+    C.io_chain(ctx, both[:n], tok, ph, [0, n], out=both[n:])
+    roots, trees = C.build_trees(ctx, both, [0, n, 2 * n], keep_trees=True, roots_out=digests[:2])
+    digests[2].copy_(ph[0])
+    seeds = ctx.to_device(np.frombuffer(seed, dtype=np.uint8).reshape(1, 32))
+    digests[3:4].copy_(C.seed_commitments(ctx, seeds))
+    kv_roots = kv_trees = None
+    n_kv_layers = 0
+    if kv_cache is not None:
+        if len(kv_cache.seq_lens) != 1:
+            raise ValueError("kv_cache must describe exactly the request's one sequence")
+        r, kv_trees = C.kv_commit(ctx, kv_cache, keep_trees=True)
+        kv_roots = r[0]
+        n_kv_layers = len(kv_cache.k_layers)
+    return handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers, **extra)
+
+
+def _wrap_rows(n_tokens, rows, n_prompt_tokens, which):
+    """Row index per token for an optional per-token list (prover/src/lib.rs:367-390)."""
+    if which == "logits":
+        gen_start = max(0, n_prompt_tokens - 1) if n_prompt_tokens is not None else 0
+        return [t - gen_start if (t >= gen_start and t - gen_start < rows) else -1 for t in range(n_tokens)]
+    return [t if t < rows else -1 for t in range(n_tokens)]
+
+
+def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_sizes, token_ids, prompt,
+                                 sampling_seed, manifest=None, weight_provider=None, final_residuals=None,
+                                 n_prompt_tokens=None, x_attn_inputs=None, lp_hidden_bf16=None,
+                                 captured_logits_f32=None, *, kv_cache: Optional[C.KvCacheView] = None,
+                                 ctx: Optional[C.Context] = None) -> MinimalBatchStateHandle:
+    """V4 commitment from minimal captures (verilm-py/src/lib.rs:800-985)."""
+    ctx = ctx or C.Context()
+    seed = _check_common(token_ids, sampling_seed, manifest)
+    fwd_batch_sizes = [int(b) for b in fwd_batch_sizes]
+    n_layers = int(n_layers)
+    scales_h = scales if (isinstance(scales, torch.Tensor) and scales.is_cuda) else _f32_host(scales)
+    expected = sum(bs * 4 * n_layers for bs in fwd_batch_sizes)
+    n_scales = scales_h.numel() if isinstance(scales_h, torch.Tensor) else scales_h.size
+    if n_scales != expected:
+        raise ValueError(f"expected {expected} scales (4 × batch_size per layer entry), got {n_scales}")
+    if len(o_proj_inputs) < len(fwd_batch_sizes) * n_layers:
+        raise ValueError("o_proj_inputs must hold one entry per (forward pass, layer)")
+    scales_d = ctx.to_device(scales_h, dtype=torch.float32)
+    a_dev = []
+    for x in o_proj_inputs[: len(fwd_batch_sizes) * n_layers]:
+        if isinstance(x, torch.Tensor) and x.is_cuda:
+            a_dev.append(x.contiguous())
+        else:
+            a_dev.append(ctx.to_device(_u8_host(x)))
+    hidden = None
+    a_rows, s_rows = [], []
+    cursor = 0
+    e = 0
+    for bs in fwd_batch_sizes:
+        ar, sr = [], []
+        for _l in range(n_layers):
+            t = a_dev[e]
+            dim = (t.numel() * t.element_size()) // bs if bs else 0
+            if hidden is None:
+                hidden = dim
+            elif dim != hidden:
+                raise ValueError("every o_proj input row must have the same length")
+            ar.append(t.data_ptr())
+            sr.append(scales_d.data_ptr() + 4 * (cursor + bs))   # the o_proj block of this entry
+            cursor += 4 * bs
+            e += 1
+        a_rows.append(ar)
+        s_rows.append(sr)
+    tok_fwd, tok_row = [], []
+    for f, bs in enumerate(fwd_batch_sizes):
+        tok_fwd += [f] * bs
+        tok_row += list(range(bs))
+    n_tok = len(tok_fwd)
+    lay = C.TraceLayout(n_layers=n_layers, hidden=hidden or 0, fwd_rows=fwd_batch_sizes, tok_fwd=tok_fwd,
+                        tok_row=tok_row, a_rows=a_rows, scale_a=s_rows, scale_stride=1)
+    keep = [a_dev, scales_d]
+    if final_residuals is not None:
+        t, rows = _rows_tensor(ctx, final_residuals, np.float32, torch.float32, "final_residuals")
+        if t is not None:
+            lay.final_residual, lay.tok_fr_row = t, _wrap_rows(n_tok, rows, n_prompt_tokens, "fr")
+            keep.append(t)
+    if lp_hidden_bf16 is not None:
+        t, rows = _rows_tensor(ctx, lp_hidden_bf16, np.uint16, torch.int16, "lp_hidden_bf16")
+        if t is not None:
+            lay.lp_hidden, lay.tok_lp_row = t, _wrap_rows(n_tok, rows, n_prompt_tokens, "lp")
+            keep.append(t)
+    if captured_logits_f32 is not None:
+        t, rows = _rows_tensor(ctx, captured_logits_f32, np.float32, torch.float32, "captured_logits_f32")
+        if t is not None:
+            lay.logits, lay.tok_logits_row = t, _wrap_rows(n_tok, rows, n_prompt_tokens, "logits")
+            keep.append(t)
+    h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle,
+                x_attn=x_attn_inputs)
+    h._inputs = keep
+    return h
+
+
+def commit_minimal_packed(packed_a, packed_scales, n_layers, hidden_dim, fwd_batch_sizes, token_ids, prompt,
+                          sampling_seed, manifest=None, weight_provider=None, packed_final_res=None,
+                          final_res_dim=0, n_prompt_tokens=None, *, kv_cache: Optional[C.KvCacheView] = None,
+                          ctx: Optional[C.Context] = None) -> PackedBatchStateHandle:
+    """V4 commitment from packed buffers (verilm-py/src/lib.rs:1189-1310)."""
+    ctx = ctx or C.Context()
+    seed = _check_common(token_ids, sampling_seed, manifest)
+    fwd_batch_sizes = [int(b) for b in fwd_batch_sizes]
+    n_layers, hidden_dim = int(n_layers), int(hidden_dim)
+    n_tok = sum(fwd_batch_sizes)
+    if n_tok != len(token_ids):
+        raise ValueError("token count must match token_ids")
+    a = packed_a if (isinstance(packed_a, torch.Tensor) and packed_a.is_cuda) else ctx.to_device(_u8_host(packed_a))
+    if a.numel() * a.element_size() != n_tok * n_layers * hidden_dim:
+        raise ValueError(f"packed_a length ({a.numel() * a.element_size()}) != expected "
+                         f"({n_tok} tokens × {n_layers} layers × {hidden_dim} dim)")
+    s = packed_scales if (isinstance(packed_scales, torch.Tensor) and packed_scales.is_cuda) else _f32_host(packed_scales)
+    n_s = s.numel() if isinstance(s, torch.Tensor) else s.size
+    if n_s != n_tok * n_layers * 4:
+        raise ValueError("scale rearrangement consumed wrong number of values")
+    s = ctx.to_device(s, dtype=torch.float32)
+    a_rows, s_rows = [], []
+    cum = 0
+    cursor = 0
+    for bs in fwd_batch_sizes:
+        ar, sr = [], []
+        for l in range(n_layers):
+            ar.append(a.data_ptr() + (cum * n_layers + l * bs) * hidden_dim)
+            sr.append(s.data_ptr() + 4 * (cursor + bs))   # drain order: [qkv | o_proj | gate | down] x bs
+            cursor += 4 * bs
+        a_rows.append(ar)
+        s_rows.append(sr)
+        cum += bs
+    tok_fwd, tok_row = [], []
+    for f, bs in enumerate(fwd_batch_sizes):
+        tok_fwd += [f] * bs
+        tok_row += list(range(bs))
+    lay = C.TraceLayout(n_layers=n_layers, hidden=hidden_dim, fwd_rows=fwd_batch_sizes, tok_fwd=tok_fwd,
+                        tok_row=tok_row, a_rows=a_rows, scale_a=s_rows, scale_stride=1)
+    keep = [a, s]
+    if packed_final_res is not None:
+        fr = packed_final_res if (isinstance(packed_final_res, torch.Tensor) and packed_final_res.is_cuda) \
+            else ctx.to_device(_u8_host(packed_final_res))
+        fr = fr.contiguous().view(torch.uint8)
+        if fr.numel() != n_tok * int(final_res_dim) * 4:
+            raise ValueError(f"packed_final_res length ({fr.numel()}) != expected "
+                             f"({n_tok} tokens × {final_res_dim} dim × 4)")
+        lay.final_residual = fr.view(torch.float32).view(n_tok, int(final_res_dim))
+        lay.tok_fr_row = list(range(n_tok))
+        keep.append(fr)
+    h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, PackedBatchStateHandle)
+    h._inputs = keep
+    return h

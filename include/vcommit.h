@@ -1,0 +1,259 @@
+/*
+ * vcommit.h -- C ABI of libvcommit.so, the B200 trace-commitment library.
+ *
+ * It replaces the hashing half of CommitLLM's provider-side commit
+ * (crates/verilm-prover/src/lib.rs:336-544, commit_minimal; 753-964,
+ * commit_minimal_packed) and the SHA-256 Merkle primitives it calls
+ * (crates/verilm-core/src/merkle.rs:11-123, 144-293, 553-577).  Every digest,
+ * root, opening and chain value is bit-identical to those functions on the
+ * same inputs, so the existing verifier accepts the receipts unchanged.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, status codes.  No CUDA or torch types; a
+ *     stream is passed as `void*` (a cudaStream_t, NULL = legacy default).
+ *   - Pointers documented DEVICE are read/written in place in HBM; HOST
+ *     arrays are small descriptor tables copied by the library.
+ *   - Every call is stream-ordered and asynchronous on its context's stream,
+ *     returns a vc_status and never aborts.  vc_last_error() gives the text.
+ *   - Errors: VC_EINVAL where the reference raises PyValueError or panics on
+ *     an assert (verilm-py/src/lib.rs:843-893, prover/src/lib.rs:347-351,
+ *     766-802); VC_ERANGE where merkle::prove asserts an index
+ *     (merkle.rs:80).
+ *   - Threading: one context per stream; distinct contexts may be used from
+ *     distinct host threads concurrently.
+ *   - Digests are 32 bytes in SHA-256 output byte order ([u8; 32]).
+ */
+#ifndef VCOMMIT_H
+#define VCOMMIT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VC_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VC_API __attribute__((visibility("default")))
+#else
+#define VC_API
+#endif
+
+typedef int32_t vc_status;
+#define VC_OK 0
+#define VC_EINVAL 1     /* invalid argument */
+#define VC_ENOMEM 2     /* device or host allocation failed */
+#define VC_ECUDA 3      /* a CUDA runtime call failed */
+#define VC_ETIMEDOUT 4  /* a bounded wait ran out */
+#define VC_ERANGE 5     /* index out of range */
+#define VC_ENOTSUP 6    /* layout not supported */
+
+/* Element type of K/V rows. */
+#define VC_DTYPE_BF16 0 /* raw bf16 bits, widened exactly to f64 before hashing */
+#define VC_DTYPE_F32 1  /* f32, widened exactly to f64 */
+#define VC_DTYPE_F64 2  /* f64 as the reference's KvEntry holds it */
+
+typedef struct vc_ctx vc_ctx;           /* per-stream context (scratch, staging) */
+typedef struct vc_tree_set vc_tree_set; /* device-resident Merkle trees */
+
+/* ---------------------------------------------------------------- context */
+
+/* Version of this ABI (VC_ABI_VERSION). */
+VC_API int32_t vc_abi_version(void);
+
+/* Text of the last error raised on the calling host thread. Returns the
+ * length of the message (excluding the NUL), truncating to buf_len-1. */
+VC_API size_t vc_last_error(char* buf, size_t buf_len);
+
+/* Create a context bound to CUDA device `device` and stream `stream`. */
+VC_API vc_status vc_ctx_create(int32_t device, void* stream, vc_ctx** out);
+VC_API vc_status vc_ctx_destroy(vc_ctx* ctx);
+/* Wait for the context's stream, polling, for at most timeout_ms
+ * milliseconds (<= 0: no limit). VC_ETIMEDOUT when the limit is reached.
+ * VC_ERANGE if a kernel of this context found a device-side index out of
+ * range since the last sync (its output is then unspecified). */
+VC_API vc_status vc_ctx_sync(vc_ctx* ctx, int32_t timeout_ms);
+
+/* ------------------------------------------------------------- KV commit */
+
+/*
+ * Where the K and V rows live.  The row of (layer l, sequence s, position p)
+ * is the kv_dim = n_kv_heads * head_dim elements
+ *
+ *   base_l + page * stride_page + slot * stride_row + h * stride_head + d
+ *
+ * for head h in [0, n_kv_heads), d in [0, head_dim), with
+ *   paged      (block_tables != NULL): page = block_tables[s * max_blocks_per_seq
+ *              + p / block_size], slot = p % block_size;
+ *   contiguous (block_tables == NULL): page = 0, slot = seq_row_offset[s] + p.
+ * Strides are in elements.  vLLM's flash layout [pages, block, heads, dim] is
+ * stride_page = block*kv_dim, stride_row = kv_dim, stride_head = head_dim.
+ *
+ * K concatenates heads head-major, the order rope.rs:95-98 uses for
+ * kv_dim = h * d_head + i, and so does V.
+ */
+typedef struct vc_kv_desc {
+    int32_t n_layers;      /* layers in this call */
+    int32_t layer_base;    /* leaf layer index = layer_base + l (layer sharding) */
+    int32_t n_kv_heads;
+    int32_t head_dim;
+    int32_t dtype;         /* VC_DTYPE_* */
+    int32_t n_seqs;
+    const int32_t* seq_lens;          /* HOST [n_seqs], each >= 1 */
+    const int64_t* seq_row_offset;    /* HOST [n_seqs], contiguous layout; NULL = prefix sum of seq_lens */
+    const int32_t* block_tables;      /* DEVICE [n_seqs * max_blocks_per_seq] or NULL */
+    int32_t block_size;
+    int32_t max_blocks_per_seq;
+    int64_t stride_page;
+    int64_t stride_row;
+    int64_t stride_head;
+    int64_t cache_elems;              /* elements in each layer's K (and V) buffer, > 0:
+                                         every row is bounds-checked against it (rows
+                                         of a paged cache on the device; a bad page id
+                                         is reported by vc_ctx_sync as VC_ERANGE) */
+    const void* const* k_layers;      /* HOST [n_layers] DEVICE base pointers */
+    const void* const* v_layers;      /* HOST [n_layers] DEVICE base pointers */
+} vc_kv_desc;
+
+/*
+ * Per-layer KV Merkle roots: hot loop C of commit_minimal
+ * (crates/verilm-prover/src/lib.rs:449-482).  Leaf (l, p) is
+ * merkle::hash_kv_entry(layer_base + l, p, f64(K row), f64(V row))
+ * (merkle.rs:285-293); each (sequence, layer) gets one merkle::build_tree
+ * (merkle.rs:11-48) over positions 0..seq_lens[s].
+ *
+ * kv_roots_dev: DEVICE [n_seqs][n_layers][32] -- sequence s's kv_roots are the
+ *   n_layers consecutive roots, the layout of BatchCommitment.kv_roots
+ *   (types.rs:1753-1758).
+ * trees_out: if non-NULL, receives every node of every tree (for openings);
+ *   tree index = s * n_layers + l.  Free with vc_tree_set_free.
+ */
+VC_API vc_status vc_kv_commit(vc_ctx* ctx, const vc_kv_desc* desc, uint8_t* kv_roots_dev,
+                       vc_tree_set** trees_out);
+
+/* ----------------------------------------------------------- trace leaves */
+
+/*
+ * Retained-state ("trace") leaves, hot loop A of commit_minimal
+ * (prover/src/lib.rs:367-393): per token
+ *   base = hash_retained_state_direct  (merkle.rs:144-161)
+ *   then the optional wraps of merkle.rs:170-241, each applied when the
+ *   token's row index for it is >= 0:
+ *     "vi-retained-fr-v1"     || base || f32le[final_residual]
+ *     "vi-retained-lp-v1"     || prev || u16le[lp_hidden_bf16]
+ *     "vi-retained-logits-v1" || prev || f32le[captured_logits]
+ *
+ * Token t's activation rows come from forward pass tok_fwd[t], batch row
+ * tok_row[t]: a_i8 of layer l at a_rows[f * n_layers + l] + row * hidden, and
+ * scale_a at scale_a[f * n_layers + l][row * scale_stride].  This covers both
+ * reference layouts: the per-(fwd, layer) buffers of
+ * commit_minimal_from_captures (verilm-py/src/lib.rs:800-885) and
+ * commit_minimal_packed's packed_a / packed_scales (prover/src/lib.rs:601-605).
+ *
+ * x_attn_rows / scale_x_attn non-NULL binds the optional "0x01 || x_attn_i8 ||
+ * f32le(scale_x_attn)" field; NULL hashes the 0x00 marker, as the
+ * reference's production path does (prover/src/lib.rs:162-167).
+ */
+typedef struct vc_trace_desc {
+    int32_t n_tokens;
+    int32_t n_layers;
+    int32_t hidden;                      /* bytes per a_i8 (and x_attn) row */
+    int32_t n_fwd;
+    const int32_t* fwd_rows;             /* HOST [n_fwd]: batch rows of each forward pass */
+    const int32_t* tok_fwd;              /* HOST [n_tokens] */
+    const int32_t* tok_row;              /* HOST [n_tokens] */
+    const void* const* a_rows;           /* HOST [n_fwd * n_layers] DEVICE i8 */
+    const void* const* scale_a;          /* HOST [n_fwd * n_layers] DEVICE f32 */
+    int64_t scale_stride;                /* f32 elements between batch rows */
+    const void* const* x_attn_rows;      /* HOST [n_fwd * n_layers] DEVICE i8, or NULL */
+    const void* const* scale_x_attn;     /* HOST [n_fwd * n_layers] DEVICE f32, or NULL */
+    int64_t scale_x_stride;
+    /* optional wraps: DEVICE row-major arrays of *_rows rows (stride in
+     * elements) + HOST per-token row index (-1: not bound for that token) */
+    const void* final_residual;  int32_t fr_dim;  int32_t fr_rows;     int64_t fr_stride;
+    const int32_t* tok_fr_row;
+    const void* lp_hidden;       int32_t lp_dim;  int32_t lp_rows;     int64_t lp_stride;
+    const int32_t* tok_lp_row;
+    const void* logits;          int32_t vocab;   int32_t logits_rows; int64_t logits_stride;
+    const int32_t* tok_logits_row;
+} vc_trace_desc;
+
+/* leaves_dev: DEVICE [n_tokens][32]. */
+VC_API vc_status vc_trace_leaves(vc_ctx* ctx, const vc_trace_desc* desc, uint8_t* leaves_dev);
+
+/* ---------------------------------------------------------------- IO chain */
+
+/*
+ * IO chains (prover/src/lib.rs:403-410): for each sequence s over its tokens
+ * t in [tok_off[s], tok_off[s+1]):
+ *   prev = io_genesis_v4(prompt_hash[s])                   (merkle.rs:572-577)
+ *   io[t] = io_hash_v4(leaves[t], token_ids[t], prev)      (merkle.rs:250-257)
+ * tok_off: HOST [n_seqs + 1]; leaves_dev, io_dev: DEVICE [n_tokens][32];
+ * token_ids_dev: DEVICE u32 [n_tokens]; prompt_hash_dev: DEVICE [n_seqs][32].
+ */
+VC_API vc_status vc_io_chain(vc_ctx* ctx, int32_t n_seqs, const int64_t* tok_off,
+                      const uint8_t* leaves_dev, const uint32_t* token_ids_dev,
+                      const uint8_t* prompt_hash_dev, uint8_t* io_dev);
+
+/* hash_prompt (merkle.rs:561-566) of n prompts; prompt i is the bytes
+ * [off[i], off[i+1]) of prompts_dev.  off: HOST [n + 1]; out: DEVICE [n][32]. */
+VC_API vc_status vc_prompt_hash(vc_ctx* ctx, int32_t n, const uint8_t* prompts_dev,
+                         const int64_t* off, uint8_t* out_dev);
+
+/* hash_seed (merkle.rs:553-558) of n 32-byte seeds: DEVICE [n][32] -> [n][32]. */
+VC_API vc_status vc_seed_commitment(vc_ctx* ctx, int32_t n, const uint8_t* seeds_dev,
+                             uint8_t* out_dev);
+
+/* ------------------------------------------------------------- Merkle trees */
+
+/*
+ * merkle::build_tree (merkle.rs:11-48) over n_trees independent leaf ranges:
+ * tree i has the leaves [leaf_off[i], leaf_off[i+1]) of leaves_dev (>= 1 leaf).
+ * leaf_off: HOST [n_trees + 1]; roots_dev: DEVICE [n_trees][32];
+ * trees_out: optional, as for vc_kv_commit.
+ */
+VC_API vc_status vc_build_trees(vc_ctx* ctx, int32_t n_trees, const int64_t* leaf_off,
+                         const uint8_t* leaves_dev, uint8_t* roots_dev,
+                         vc_tree_set** trees_out);
+
+/*
+ * merkle::prove (merkle.rs:79-99) for n openings (tree[i], leaf[i]), HOST
+ * arrays.  siblings_dev: DEVICE [n][max_depth][32], bottom-up, the order of
+ * MerkleProof.siblings (merkle.rs:303-307); depth_out: HOST [n], the number
+ * of siblings of each proof (log2 of the tree's padded size).
+ * VC_ERANGE if a leaf index is >= the tree's leaf count or a tree is unknown.
+ */
+VC_API vc_status vc_prove(vc_ctx* ctx, const vc_tree_set* trees, int32_t n, const int32_t* tree,
+                   const uint32_t* leaf, uint8_t* siblings_dev, int32_t max_depth,
+                   int32_t* depth_out);
+
+/* Shape of a tree set: number of trees. */
+VC_API int32_t vc_tree_set_count(const vc_tree_set* trees);
+/*
+ * The node array of one tree, laid out as MerkleTree.nodes (merkle.rs:16-39):
+ * level 0 (padded_size leaves, zero padded), then each parent level, root
+ * last; 2 * padded_size - 1 nodes of 32 bytes.  *nodes_dev is DEVICE memory
+ * owned by the tree set.
+ */
+VC_API vc_status vc_tree_nodes(const vc_tree_set* trees, int32_t tree, const uint8_t** nodes_dev,
+                        int64_t* n_leaves, int64_t* padded_size);
+VC_API vc_status vc_tree_set_free(vc_tree_set* trees);
+
+/* --------------------------------------------------------- measurement aid */
+
+/*
+ * Integer-ALU peak probe: runs a register-only loop of 32-bit funnel shifts,
+ * 3-input logic ops and 3-input adds in SHA-256's proportions across the whole
+ * device for `iters` iterations and reports executed 32-bit ops per second
+ * (device-timed).  variant 0: SHA-256 mix; 1: funnel shift only;
+ * 2: lop3 only; 3: iadd3 only.
+ */
+VC_API vc_status vc_int_peak(vc_ctx* ctx, int32_t variant, int64_t iters, double* ops_per_s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VCOMMIT_H */

@@ -1,0 +1,429 @@
+"""The oracle: a CPU restatement of CommitLLM's trace-commitment encodings.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the product path (``commitllm_b200``)
+imports this module; only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` leg of ``bench.py`` use it, as the checker.
+
+Every function restates one function of the reference (lambdaclass/CommitLLM)
+and cites the file:line it follows.  The hash is FIPS 180-4 SHA-256, the
+algorithm of the ``sha2`` crate v0.10.9 that ``verilm-core`` pins
+(``crates/verilm-core/Cargo.toml:7``, ``Cargo.lock:783-784``); Python's
+``hashlib.sha256`` computes the same function.  All integers are encoded
+little-endian, as the reference's ``to_le_bytes`` calls do.
+
+Pinned against the reference's golden vectors in ``tests/golden/`` (see
+``tests/test_oracle_golden.py``): the ``golden_e2e_verify`` merkle_root /
+io_root pins and the two frozen ``v4_audit_*.bin`` receipts.
+"""
+from __future__ import annotations
+
+import hashlib
+import struct
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+ZERO32 = bytes(32)
+
+
+def sha256(*parts: bytes) -> bytes:
+    h = hashlib.sha256()
+    for p in parts:
+        h.update(p)
+    return h.digest()
+
+
+# ---------------------------------------------------------------------------
+# Merkle tree: crates/verilm-core/src/merkle.rs:11-123
+# ---------------------------------------------------------------------------
+
+def hash_pair(left: bytes, right: bytes) -> bytes:
+    """``hash_pair`` (merkle.rs:118-123): SHA256(left || right), no tag."""
+    return sha256(left, right)
+
+
+def hash_leaf(data: bytes) -> bytes:
+    """``hash_leaf`` (merkle.rs:126-130)."""
+    return sha256(data)
+
+
+def next_pow2(n: int) -> int:
+    p = 1
+    while p < n:
+        p <<= 1
+    return p
+
+
+@dataclass
+class MerkleTree:
+    """``MerkleTree`` (merkle.rs:295-301): nodes level-concatenated bottom-up."""
+    nodes: List[bytes]
+    n_leaves: int
+    padded_size: int
+    root: bytes
+
+
+@dataclass
+class MerkleProof:
+    """``MerkleProof`` (merkle.rs:303-307): siblings bottom-up."""
+    leaf_index: int
+    siblings: List[bytes] = field(default_factory=list)
+
+
+def build_tree(leaves: Sequence[bytes]) -> MerkleTree:
+    """``build_tree`` (merkle.rs:11-48).
+
+    Pads level 0 to the next power of two with all-zero leaves (padding
+    happens at level 0 only), then hashes pairs level by level.
+    """
+    if len(leaves) == 0:
+        raise ValueError("need at least one leaf")
+    n = next_pow2(len(leaves))
+    nodes = list(leaves) + [ZERO32] * (n - len(leaves))
+    start, size = 0, n
+    while size > 1:
+        for i in range(0, size, 2):
+            nodes.append(hash_pair(nodes[start + i], nodes[start + i + 1]))
+        start += size
+        size //= 2
+    return MerkleTree(nodes=nodes, n_leaves=len(leaves), padded_size=n, root=nodes[-1])
+
+
+def compute_root(leaves: Sequence[bytes]) -> bytes:
+    """``compute_root`` (merkle.rs:55-76): same root as ``build_tree``."""
+    if len(leaves) == 0:
+        raise ValueError("need at least one leaf")
+    level = list(leaves) + [ZERO32] * (next_pow2(len(leaves)) - len(leaves))
+    while len(level) > 1:
+        level = [hash_pair(level[i], level[i + 1]) for i in range(0, len(level), 2)]
+    return level[0]
+
+
+def prove(tree: MerkleTree, index: int) -> MerkleProof:
+    """``prove`` (merkle.rs:79-99)."""
+    if not (0 <= index < tree.n_leaves):
+        raise IndexError("leaf index out of range")
+    sib = []
+    idx, start, size = index, 0, tree.padded_size
+    while size > 1:
+        s = idx + 1 if idx % 2 == 0 else idx - 1
+        sib.append(tree.nodes[start + s])
+        start += size
+        size //= 2
+        idx //= 2
+    return MerkleProof(leaf_index=index, siblings=sib)
+
+
+def verify(root: bytes, leaf: bytes, proof: MerkleProof) -> bool:
+    """``verify`` (merkle.rs:102-116)."""
+    cur, idx = leaf, proof.leaf_index
+    for s in proof.siblings:
+        cur = hash_pair(cur, s) if idx % 2 == 0 else hash_pair(s, cur)
+        idx //= 2
+    return cur == root
+
+
+def zero_subtree_roots(max_height: int) -> List[bytes]:
+    """Z_0 = 0^32, Z_{k+1} = H(Z_k || Z_k): the root of an all-padding subtree.
+
+    Not a reference function; it is what ``build_tree`` computes for a
+    subtree whose leaves are all zero padding (merkle.rs:22-39).
+    """
+    z = [ZERO32]
+    for _ in range(max_height):
+        z.append(hash_pair(z[-1], z[-1]))
+    return z
+
+
+# ---------------------------------------------------------------------------
+# Leaf encodings: crates/verilm-core/src/merkle.rs:144-293
+# ---------------------------------------------------------------------------
+
+def bf16_to_f64(bits: np.ndarray) -> np.ndarray:
+    """Widen raw bf16 bit patterns to f64, exactly.
+
+    bf16 -> f32 is a 16-bit left shift; f32 -> f64 is numpy's (IEEE) widening,
+    which is exact for every finite value including subnormals.  NaNs keep their
+    payload with the quiet bit set.  This is the value set a KV entry holds when
+    the K/V cache row is bf16 (``KvEntry`` is ``Vec<f64>``, types.rs:1244-1251).
+    """
+    b = np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16
+    f32 = b.view(np.float32)
+    with np.errstate(invalid="ignore"):
+        out = f32.astype(np.float64)
+    # numpy's cast of a signalling NaN is platform defined: force the quiet bit
+    # explicitly so the encoding is pinned (sign | 0x7FF | quiet | payload<<29).
+    nan = np.isnan(f32)
+    if nan.any():
+        u = b[nan].astype(np.uint64)
+        sign = (u >> 31) << 63
+        payload = (u & 0x7FFFFF) << 29
+        quiet = np.uint64(1) << np.uint64(51)
+        out_bits = out.view(np.uint64).copy()
+        out_bits[nan] = sign | (np.uint64(0x7FF) << np.uint64(52)) | quiet | payload
+        out = out_bits.view(np.float64)
+    return out
+
+
+def f32_to_f64(vals: np.ndarray) -> np.ndarray:
+    """Widen f32 to f64 with the same NaN rule as :func:`bf16_to_f64`."""
+    b = np.ascontiguousarray(vals, dtype=np.float32).view(np.uint32)
+    f32 = b.view(np.float32)
+    with np.errstate(invalid="ignore"):
+        out = f32.astype(np.float64)
+    nan = np.isnan(f32)
+    if nan.any():
+        u = b[nan].astype(np.uint64)
+        sign = (u >> 31) << 63
+        payload = (u & 0x7FFFFF) << 29
+        quiet = np.uint64(1) << np.uint64(51)
+        out_bits = out.view(np.uint64).copy()
+        out_bits[nan] = sign | (np.uint64(0x7FF) << np.uint64(52)) | quiet | payload
+        out = out_bits.view(np.float64)
+    return out
+
+
+def hash_kv_entry(layer: int, position: int, k_roped: np.ndarray, v_deq: np.ndarray) -> bytes:
+    """``hash_kv_entry`` (merkle.rs:285-293) with ``hash_f64_into`` (274-278).
+
+    SHA256("vi-kv-v1" || u32le(layer) || u32le(pos) || f64le[k] || f64le[v]).
+    """
+    k = np.ascontiguousarray(k_roped, dtype="<f8")
+    v = np.ascontiguousarray(v_deq, dtype="<f8")
+    return sha256(b"vi-kv-v1", struct.pack("<II", layer & 0xFFFFFFFF, position & 0xFFFFFFFF),
+                  k.tobytes(), v.tobytes())
+
+
+@dataclass
+class RetainedLayerState:
+    """``RetainedLayerState`` (types.rs:1201-1219)."""
+    a: bytes                       # i8 bytes
+    scale_a: float                 # f32
+    x_attn_i8: Optional[bytes] = None
+    scale_x_attn: Optional[float] = None
+
+
+def _f32le(x: float) -> bytes:
+    return struct.pack("<f", x)
+
+
+def hash_retained_state_direct(layers: Sequence[RetainedLayerState]) -> bytes:
+    """``hash_retained_state_direct`` (merkle.rs:144-161).
+
+    SHA256("vi-retained-v3" || for each layer: a || f32le(scale_a) ||
+    (0x01 || x_attn_i8 || f32le(scale_x_attn) when both are Some, else 0x00)).
+    """
+    h = hashlib.sha256(b"vi-retained-v3")
+    for ls in layers:
+        h.update(bytes(ls.a))
+        h.update(_f32le(ls.scale_a))
+        if ls.x_attn_i8 is not None and ls.scale_x_attn is not None:
+            h.update(b"\x01")
+            h.update(bytes(ls.x_attn_i8))
+            h.update(_f32le(ls.scale_x_attn))
+        else:
+            h.update(b"\x00")
+    return h.digest()
+
+
+def _f32_bytes(arr) -> bytes:
+    return np.ascontiguousarray(arr, dtype="<f4").tobytes()
+
+
+def hash_retained_with_residual(layers, final_residual=None) -> bytes:
+    """``hash_retained_with_residual`` (merkle.rs:170-185)."""
+    base = hash_retained_state_direct(layers)
+    if final_residual is None:
+        return base
+    return sha256(b"vi-retained-fr-v1", base, _f32_bytes(final_residual))
+
+
+def hash_retained_with_lp_hidden(layers, final_residual=None, lp_hidden_bf16=None) -> bytes:
+    """``hash_retained_with_lp_hidden`` (merkle.rs:195-215): u16le bf16 bits."""
+    base = hash_retained_with_residual(layers, final_residual)
+    if lp_hidden_bf16 is None:
+        return base
+    lp = np.ascontiguousarray(lp_hidden_bf16, dtype="<u2").tobytes()
+    return sha256(b"vi-retained-lp-v1", base, lp)
+
+
+def hash_retained_with_captured_logits(layers, final_residual=None, lp_hidden_bf16=None,
+                                       captured_logits_f32=None) -> bytes:
+    """``hash_retained_with_captured_logits`` (merkle.rs:224-241)."""
+    base = hash_retained_with_lp_hidden(layers, final_residual, lp_hidden_bf16)
+    if captured_logits_f32 is None:
+        return base
+    return sha256(b"vi-retained-logits-v1", base, _f32_bytes(captured_logits_f32))
+
+
+# ---------------------------------------------------------------------------
+# IO chain and bindings: merkle.rs:250-257, 553-577
+# ---------------------------------------------------------------------------
+
+def io_hash_v4(leaf_hash: bytes, token_id: int, prev_io_hash: bytes) -> bytes:
+    """``io_hash_v4`` (merkle.rs:250-257)."""
+    return sha256(b"vi-io-v4", leaf_hash, struct.pack("<I", token_id & 0xFFFFFFFF), prev_io_hash)
+
+
+def hash_seed(seed: bytes) -> bytes:
+    """``hash_seed`` (merkle.rs:553-558)."""
+    return sha256(b"vi-seed-v1", seed)
+
+
+def hash_prompt(prompt: bytes) -> bytes:
+    """``hash_prompt`` (merkle.rs:561-566)."""
+    return sha256(b"vi-prompt-v1", prompt)
+
+
+def io_genesis_v4(prompt_hash: bytes) -> bytes:
+    """``io_genesis_v4`` (merkle.rs:572-577)."""
+    return sha256(b"vi-io-genesis-v4", prompt_hash)
+
+
+def io_chain(trace_leaves: Sequence[bytes], token_ids: Sequence[int], prompt: bytes) -> List[bytes]:
+    """The IO chain loop of ``commit_minimal`` (verilm-prover/src/lib.rs:403-410)."""
+    prev = io_genesis_v4(hash_prompt(prompt))
+    out = []
+    for leaf, tok in zip(trace_leaves, token_ids):
+        prev = io_hash_v4(leaf, tok, prev)
+        out.append(prev)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# commit_minimal: crates/verilm-prover/src/lib.rs:336-499 (hashing parts)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Commitment:
+    """The hashed fields of ``BatchCommitment`` (types.rs:1710-1759)."""
+    merkle_root: bytes
+    io_root: bytes
+    n_tokens: int
+    prompt_hash: bytes
+    seed_commitment: bytes
+    n_prompt_tokens: Optional[int]
+    kv_roots: List[bytes]
+    trace_leaves: List[bytes]
+    io_hashes: List[bytes]
+    trace_tree: MerkleTree
+    io_tree: MerkleTree
+    kv_trees: List[MerkleTree]
+
+
+def trace_leaves_of(all_retained, final_residuals=None, lp_hidden_bf16=None,
+                    captured_logits_f32=None, n_prompt_tokens=None) -> List[bytes]:
+    """Hot loop A of ``commit_minimal`` (prover/src/lib.rs:367-393).
+
+    ``captured_logits_f32[j]`` binds to token ``gen_start + j`` with
+    ``gen_start = n_prompt_tokens - 1`` (saturating); the optional lists bind
+    only to indices they have (``.get(i)``).
+    """
+    gen_start = max(0, (n_prompt_tokens or 0) - 1) if n_prompt_tokens is not None else 0
+    leaves = []
+    for i, layers in enumerate(all_retained):
+        fr = final_residuals[i] if final_residuals is not None and i < len(final_residuals) else None
+        lp = lp_hidden_bf16[i] if lp_hidden_bf16 is not None and i < len(lp_hidden_bf16) else None
+        cl = None
+        if i >= gen_start and captured_logits_f32 is not None and (i - gen_start) < len(captured_logits_f32):
+            cl = captured_logits_f32[i - gen_start]
+        leaves.append(hash_retained_with_captured_logits(layers, fr, lp, cl))
+    return leaves
+
+
+def kv_tree_for_layer(layer_idx: int, k_rows: np.ndarray, v_rows: np.ndarray) -> MerkleTree:
+    """Hot loop C of ``commit_minimal`` (prover/src/lib.rs:449-482) for one layer.
+
+    ``k_rows``/``v_rows`` are f64 ``[n_pos, kv_dim]``; leaf ``pos`` is
+    ``hash_kv_entry(layer_idx, pos, k[pos], v[pos])``.
+    """
+    leaves = [hash_kv_entry(layer_idx, p, k_rows[p], v_rows[p]) for p in range(k_rows.shape[0])]
+    return build_tree(leaves)
+
+
+def commit_minimal(all_retained, token_ids, prompt: bytes, sampling_seed: bytes,
+                   final_residuals=None, kv_transcripts=None, lp_hidden_bf16=None,
+                   captured_logits_f32=None, n_prompt_tokens=None) -> Commitment:
+    """``commit_minimal`` (prover/src/lib.rs:336-499) minus the manifest.
+
+    ``kv_transcripts`` is ``[layer] -> (k f64 [n_pos, kv_dim], v f64 [n_pos, kv_dim])``.
+    """
+    if len(all_retained) != len(token_ids):
+        raise ValueError("retained state count must match token_ids")
+    leaves = trace_leaves_of(all_retained, final_residuals, lp_hidden_bf16,
+                             captured_logits_f32, n_prompt_tokens)
+    ios = io_chain(leaves, token_ids, prompt)
+    trace_tree = build_tree(leaves)
+    io_tree = build_tree(ios)
+    kv_trees = []
+    if kv_transcripts is not None:
+        for l, (k, v) in enumerate(kv_transcripts):
+            kv_trees.append(kv_tree_for_layer(l, k, v))
+    return Commitment(
+        merkle_root=trace_tree.root, io_root=io_tree.root, n_tokens=len(all_retained),
+        prompt_hash=hash_prompt(prompt), seed_commitment=hash_seed(sampling_seed),
+        n_prompt_tokens=n_prompt_tokens, kv_roots=[t.root for t in kv_trees],
+        trace_leaves=leaves, io_hashes=ios, trace_tree=trace_tree, io_tree=io_tree,
+        kv_trees=kv_trees)
+
+
+def build_retained_from_captures(o_proj_inputs: Sequence[bytes], scales: Sequence[float],
+                                 n_layers: int, fwd_batch_sizes: Sequence[int]):
+    """``commit_minimal_from_captures``' scale split (verilm-py/src/lib.rs:843-885)
+    followed by ``build_retained_from_captures`` (prover/src/lib.rs:128-186).
+
+    ``scales`` holds, per (fwd pass, layer), ``[B qkv | B o_proj | B gate | B down]``;
+    ``scale_a`` is the o_proj block.  ``x_attn_i8`` is never placed in the
+    retained state (prover/src/lib.rs:162-167).
+    """
+    out = []
+    cursor = 0
+    entry = 0
+    per_fwd = []
+    for bs in fwd_batch_sizes:
+        layer_rows = []
+        for _l in range(n_layers):
+            a = bytes(o_proj_inputs[entry])
+            s_o = scales[cursor + bs: cursor + 2 * bs]
+            cursor += 4 * bs
+            layer_rows.append((a, s_o))
+            entry += 1
+        per_fwd.append((bs, layer_rows))
+    for bs, layer_rows in per_fwd:
+        for b in range(bs):
+            layers = []
+            for a, s_o in layer_rows:
+                dim = len(a) // bs
+                layers.append(RetainedLayerState(a=a[b * dim:(b + 1) * dim], scale_a=float(np.float32(s_o[b]))))
+            out.append(layers)
+    return out
+
+
+def packed_token_layers(packed_a: bytes, packed_scales: np.ndarray, n_layers: int, hidden_dim: int,
+                        fwd_batch_sizes: Sequence[int]):
+    """``PackedBatchState::hash_token``'s addressing (prover/src/lib.rs:639-681).
+
+    a(f, l, b) at ``cum[f]*L*H + l*bs_f*H + b*H``; scale_a at
+    ``packed_scales[(t*L + l)*4 + 1]``.
+    """
+    scales = np.asarray(packed_scales, dtype=np.float32)
+    out = []
+    cum = 0
+    t = 0
+    for bs in fwd_batch_sizes:
+        for b in range(bs):
+            layers = []
+            for l in range(n_layers):
+                off = cum * n_layers * hidden_dim + l * bs * hidden_dim + b * hidden_dim
+                layers.append(RetainedLayerState(a=bytes(packed_a[off:off + hidden_dim]),
+                                                 scale_a=float(scales[(t * n_layers + l) * 4 + 1])))
+            out.append(layers)
+            t += 1
+        cum += bs
+    return out
+
+
+def sha256_blocks(msg_len: int) -> int:
+    """FIPS 180-4 block count for a message of ``msg_len`` bytes."""
+    return (msg_len + 9 + 63) // 64

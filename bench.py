@@ -53,12 +53,16 @@ def algorithmic(w):
 
 
 class Clocks:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons; summary() keeps the
+    samples taken between mark_start() and mark_end() (host monotonic time)."""
+
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
         self.rows = []
         self._p = None
+        self.t_start = self.t_end = None
 
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -66,20 +70,30 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self._p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                        "--format=csv,noheader,nounits", "-lms", "100"],
+                                        "--format=csv,noheader,nounits", "-lms", "50"],
                                        stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            deadline = time.monotonic() + 10
+            while not self.rows and time.monotonic() < deadline:
+                time.sleep(0.02)
         except OSError:
             self._p = None
         return self
 
     def _read(self):
         for line in self._p.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            self.rows.append((time.monotonic(), [x.strip() for x in line.split(",")]))
+
+    def mark_start(self):
+        self.t_start = time.monotonic()
+
+    def mark_end(self):
+        self.t_end = time.monotonic()
 
     def __exit__(self, *a):
         if self._p:
+            time.sleep(0.06)
             self._p.terminate()
             try:
                 self._p.wait(timeout=5)
@@ -87,17 +101,23 @@ class Clocks:
                 self._p.kill()
 
     def summary(self):
-        sm = sorted(float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit())
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        rows = [r for t, r in self.rows if len(r) > 8 and (self.t_start is None or self.t_start <= t <= self.t_end)]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = sorted(v for v in (num(r[1]) for r in rows) if v is not None)
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        pw = [v for v in (num(r[3]) for r in rows) if v is not None]
         reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) > 8:
-                for i, n in enumerate(names):
-                    if r[5 + i].lower().startswith("active"):
-                        reasons.add(n)
+        for r in rows:
+            for i, n in enumerate(self.NAMES):
+                if r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx[0] if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(pw) if pw else None}
 
 
 def make_view(w, device, seed):
@@ -201,7 +221,7 @@ def run_reference(args, w, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -210,6 +230,9 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = WORKLOADS[args.workload]
+    if args.steps is None:
+        # about a second of timed work, so the clock sampler sees the region
+        args.steps = {"c2": 400, "c3": 40, "c5": 8}[args.workload] if args.impl == "ours" else 10
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -267,11 +290,14 @@ def main():
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        clk.mark_start()
         t0.record(stream)
         for _ in range(args.steps):
             step(True)
         t1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_end()
     ctx.sync(timeout_ms=600000)
     total_ms = t0.elapsed_time(t1)
     if world > 1:

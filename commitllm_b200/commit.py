@@ -52,7 +52,7 @@ class _DevView:
     """__cuda_array_interface__ view of library-owned device memory."""
 
     def __init__(self, ptr: int, nbytes: int, owner):
-        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, True),
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
                                          "version": 3, "strides": None}
         self._owner = owner
 
@@ -105,7 +105,10 @@ class Context:
         elif isinstance(x, (bytes, bytearray, memoryview)):
             t = torch.frombuffer(bytearray(x), dtype=torch.uint8)
         else:
-            t = torch.from_numpy(np.ascontiguousarray(x))
+            a = np.ascontiguousarray(x)
+            if not a.flags.writeable:
+                a = a.copy()
+            t = torch.from_numpy(a)
         if dtype is not None and t.dtype != dtype:
             t = t.to(dtype)
         if not t.is_cuda or t.device.index != self.device:

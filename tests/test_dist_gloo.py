@@ -1,0 +1,94 @@
+"""Sharding and the root exchange across ranks, on CPU with gloo (world size 2-4).
+
+Each rank computes its shard's kv_roots with the oracle (the stand-in for
+the GPU commit in this CPU test), the ranks all-gather them through
+``commitllm_b200.dist.gather_roots``, and every rank must end up with the
+single-process roots in (sequence, layer) order and the same root-of-roots.
+A rank that fails before the exchange makes the others fail fast (short
+process-group timeout) instead of hanging.
+"""
+import multiprocessing as mp
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+
+from commitllm_b200 import dist as D
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_shard_plan_covers_every_tree_once():
+    for S, L, W in [(1, 32, 1), (1, 32, 2), (1, 32, 8), (3, 5, 4), (32, 80, 8), (4, 80, 8), (5, 2, 3), (2, 3, 8)]:
+        plan = D.shard_plan(S, L, W)
+        assert len(plan) == W
+        seen = D.tree_order(plan, L)
+        assert sorted(seen) == [(s, l) for s in range(S) for l in range(L)]
+        assert len(seen) == len(set(seen))
+
+
+def _worker(rank, world, port, S, L, fail_rank, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        from tests import kvref
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        plan = D.shard_plan(S, L, world)
+        sh = plan[rank]
+        tr = kvref.contiguous(55, L, [9 + 3 * s for s in range(S)], 2, 8)
+        if rank == fail_rank:
+            raise RuntimeError("injected failure before the exchange")
+        # this rank's shard: sequences [b, e), layers [lb, le)
+        roots_all, _ = tr.oracle(n_threads=1, with_nodes=False)
+        local = torch.from_numpy(np.ascontiguousarray(roots_all[sh.seq_begin:sh.seq_end, sh.layer_begin:sh.layer_end]))
+        full = D.gather_roots(local.reshape(-1, 32), plan, S, L)
+        from oracle import commit_oracle as O
+        ror = O.compute_root([bytes(x) for x in full.reshape(-1, 32).numpy()])
+        q.put((rank, "ok", bytes(full.numpy().tobytes()), ror, bytes(roots_all.tobytes())))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        q.put((rank, "err", f"{type(e).__name__}: {e}", traceback.format_exc(), None))
+
+
+def _run(world, S, L, fail_rank=-1, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, S, L, fail_rank, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = []
+    for _ in range(world):
+        out.append(q.get(timeout=timeout))
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return sorted(out, key=lambda x: x[0])
+
+
+@pytest.mark.parametrize("world,S,L", [(2, 1, 6), (2, 3, 4), (4, 2, 5)])
+def test_gather_roots_reassembles_single_process_roots(world, S, L):
+    res = _run(world, S, L)
+    assert all(r[1] == "ok" for r in res), res
+    want = res[0][4]
+    for r in res:
+        assert r[2] == want              # every rank holds every kv_root, in order
+        assert r[3] == res[0][3]         # and the same root-of-roots
+
+
+def test_failed_rank_does_not_hang_the_others():
+    res = _run(2, 2, 2, fail_rank=1, timeout=180)
+    assert res[1][1] == "err" and "injected" in res[1][2]
+    assert res[0][1] == "err"            # rank 0's collective ended with an error, not a hang

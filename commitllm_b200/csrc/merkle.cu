@@ -19,6 +19,8 @@
 #include "sha256_stream.cuh"
 #include "vc_internal.h"
 
+#include <cstring>
+
 namespace vc {
 
 __host__ __device__ __forceinline__ int64_t level_off(int lp, int k) {
@@ -531,6 +533,231 @@ __global__ void prove_kernel(const uint8_t* nodes, const ProveReq* reqs, int n, 
   dst[0] = src[0];
   dst[1] = src[1];
 }
+
+
+// ---------------------------------------------------------------------------
+// Allocation-free KV commit: vc_kv_commit_noalloc.
+//
+// Some callers cannot allocate device memory at the moment they commit: a
+// serving engine that reserves all free HBM for its KV cache at start-up, an
+// allocator-less embedding, or code running where a cudaMalloc would stall
+// the device.  This variant of kv_commit_kernel needs no allocation at all:
+// its scratch (per-tree completion counters and per-chunk subtree roots) and
+// its padding-root table live in file-scope device arrays that every GPU
+// which loads the library holds until the process exits, and its descriptor
+// tables travel as one kernel argument.  The caller passes inputs and outputs
+// exactly as for vc_kv_commit; no tree nodes are kept (roots only).
+// ---------------------------------------------------------------------------
+constexpr int kNoAllocMaxSeqs = 64;
+constexpr int kNoAllocMaxLayers = 256;
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr size_t kNoAllocErrBytes = 256;                   // internal bounds flag
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(16) uint32_t g_noalloc_zero[(kMaxTreeHeight + 1) * 8];
+
+struct NoAllocArgs {
+  KvArgs kv;                                 // meta, items, k_layers, v_layers unused
+  TreeMeta meta[kNoAllocMaxSeqs];
+  int32_t chunk_off[kNoAllocMaxSeqs + 1];    // first chunk of each sequence in the grid
+  int32_t n_seqs;
+  const void* k_layers[kNoAllocMaxLayers];
+  const void* v_layers[kNoAllocMaxLayers];
+};
+
+template <int DT>
+__global__ void __launch_bounds__(kTreeThreads) kv_commit_noalloc_kernel(const __grid_constant__ NoAllocArgs na) {
+  __shared__ uint32_t sd[8][kTreeThreads];
+  const KvArgs& a = na.kv;
+  int sq = 0;
+  while (sq + 1 < na.n_seqs && na.chunk_off[sq + 1] <= int(blockIdx.x)) ++sq;
+  const TreeMeta m = na.meta[sq];
+  const int layer = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int c = 1 << m.log2_chunk;
+  const int64_t chunk = int64_t(blockIdx.x) - na.chunk_off[sq];
+  const int64_t p = chunk * c + tid;
+  if (tid < c) {
+    uint32_t d[8];
+    const int64_t row = p < m.n_leaves ? kv_row(a, m, p) : -1;
+    if (row >= 0) {
+      constexpr int esz = DT == 0 ? 2 : (DT == 1 ? 4 : 8);
+      const int64_t off = row * esz;
+      RowCursor rc;
+      rc.kb = static_cast<const char*>(na.k_layers[layer]) + off;
+      rc.vb = static_cast<const char*>(na.v_layers[layer]) + off;
+      rc.hs = a.stride_head * esz;
+      rc.cb = 8 * esz;
+      rc.cph = a.head_dim >> 3;
+      rc.nh = a.n_heads;
+      rc.sel = 0; rc.h = 0; rc.ci = 0;
+      const int kv = a.n_heads * a.head_dim;
+      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(p), rc, kv >> 2, uint32_t(16 + 16 * kv) * 8u);
+    } else {
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = 0;
+    }
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sd[w][tid] = d[w];
+  }
+  __syncthreads();
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+}
+
+}  // namespace vc
+
+#include <mutex>
+#include "../../include/vcommit.h"
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+bool g_noalloc_ready[kNoAllocMaxDevices];
+unsigned char* g_noalloc_scratch_ptr[kNoAllocMaxDevices];
+uint32_t* g_noalloc_zero_ptr[kNoAllocMaxDevices];
+
+// First call on a device: host code cannot use the arrays' names as device
+// addresses, so look the addresses up (with that device current) and fill
+// the padding-root table.  Synchronises the stream once.
+vc_status noalloc_setup(int dev, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ready[dev]) return VC_OK;
+  void* sp = nullptr;
+  void* zp = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&sp, vc::g_noalloc_scratch);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&zp, vc::g_noalloc_zero);
+  if (e != cudaSuccess) return vc::set_error(VC_ECUDA, "vc_kv_commit_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  e = vc::launch_zero_roots(static_cast<uint32_t*>(zp), stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return vc::set_error(VC_ECUDA, "vc_kv_commit_noalloc: set-up: %s", cudaGetErrorString(e));
+  g_noalloc_scratch_ptr[dev] = static_cast<unsigned char*>(sp);
+  g_noalloc_zero_ptr[dev] = static_cast<uint32_t*>(zp);
+  g_noalloc_ready[dev] = true;
+  return VC_OK;
+}
+
+}  // namespace
+
+extern "C" vc_status vc_kv_commit_noalloc(const vc_kv_desc* d, uint8_t* kv_roots_dev, int32_t* err_flag_dev,
+                                          void* stream_) {
+  using namespace vc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!d || !kv_roots_dev) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: NULL argument");
+  if (d->n_layers < 1 || d->n_seqs < 1 || d->n_kv_heads < 1 || d->head_dim < 1)
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: n_layers, n_seqs, n_kv_heads, head_dim must be >= 1");
+  if (d->n_seqs > kNoAllocMaxSeqs || d->n_layers > kNoAllocMaxLayers)
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: at most %d sequences and %d layers per call (got %d, %d)",
+                     kNoAllocMaxSeqs, kNoAllocMaxLayers, d->n_seqs, d->n_layers);
+  if (d->dtype < VC_DTYPE_BF16 || d->dtype > VC_DTYPE_F64) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: bad dtype");
+  if (!d->seq_lens || !d->k_layers || !d->v_layers) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: NULL table");
+  if (d->cache_elems <= 0 || d->stride_row < 0 || d->stride_head < 0 || d->stride_page < 0)
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: cache_elems must be > 0 and strides >= 0");
+  const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
+  const int esz = d->dtype == VC_DTYPE_BF16 ? 2 : (d->dtype == VC_DTYPE_F32 ? 4 : 8);
+  const bool paged = d->block_tables != nullptr;
+  if (paged && (d->block_size < 1 || d->max_blocks_per_seq < 1))
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: paged layout needs block_size and max_blocks_per_seq >= 1");
+  bool fast = kv % 8 == 0 && d->head_dim % 8 == 0 && (d->stride_row * esz) % 16 == 0 &&
+              (d->stride_head * esz) % 16 == 0 && (!paged || (d->stride_page * esz) % 16 == 0);
+  for (int l = 0; l < d->n_layers && fast; ++l)
+    fast = d->k_layers[l] && d->v_layers[l] && reinterpret_cast<uintptr_t>(d->k_layers[l]) % 16 == 0 &&
+           reinterpret_cast<uintptr_t>(d->v_layers[l]) % 16 == 0;
+  if (!fast)
+    return set_error(VC_ENOTSUP, "vc_kv_commit_noalloc: needs kv_dim and head_dim multiples of 8 and 16-byte aligned "
+                                 "rows (use vc_kv_commit otherwise)");
+  const int64_t row_span = int64_t(d->n_kv_heads - 1) * d->stride_head + d->head_dim;
+
+  NoAllocArgs na;
+  std::memset(&na, 0, sizeof(na));
+  int64_t acc = 0, croots = 0;
+  int32_t chunks = 0;
+  for (int s = 0; s < d->n_seqs; ++s) {
+    const int64_t n = d->seq_lens[s];
+    if (n < 1) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: seq_lens[%d] = %lld (need at least one leaf)", s, (long long)n);
+    const int64_t r0 = d->seq_row_offset ? d->seq_row_offset[s] : acc;
+    if (paged) {
+      if ((n + d->block_size - 1) / d->block_size > d->max_blocks_per_seq)
+        return set_error(VC_EINVAL, "vc_kv_commit_noalloc: seq %d needs more than max_blocks_per_seq pages", s);
+    } else if (r0 < 0 || (r0 + n - 1) * d->stride_row + row_span > d->cache_elems) {
+      return set_error(VC_EINVAL, "vc_kv_commit_noalloc: rows of seq %d exceed cache_elems", s);
+    }
+    TreeMeta& m = na.meta[s];
+    int lp = 0;
+    while ((int64_t(1) << lp) < n) ++lp;
+    const int kc = lp < kLog2TreeThreads ? lp : kLog2TreeThreads;
+    m.n_leaves = n;
+    m.log2_pad = lp;
+    m.log2_chunk = kc;
+    m.n_chunks = int32_t((n + (int64_t(1) << kc) - 1) >> kc);
+    m.node_stride = 0;
+    m.node_base = 0;
+    m.croot_stride = (int64_t(1) << lp) >> kc;
+    m.croot_base = croots;
+    croots += int64_t(d->n_layers) * m.croot_stride;
+    m.src_off = r0;
+    m.tree_base = s * d->n_layers;
+    m.seq = s;
+    na.chunk_off[s] = chunks;
+    if (int64_t(chunks) + m.n_chunks > 0x7FFFFFFF) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: too many chunks");
+    chunks += m.n_chunks;
+    acc += n;
+  }
+  na.chunk_off[d->n_seqs] = chunks;
+  na.n_seqs = d->n_seqs;
+  const int n_trees = d->n_seqs * d->n_layers;
+  const size_t counters_bytes = (size_t(n_trees) * 4 + 255) / 256 * 256;
+  const size_t need = kNoAllocErrBytes + counters_bytes + size_t(croots) * 32;
+  if (need > kNoAllocScratchBytes)
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: needs %zu bytes of scratch, the fixed maximum is %zu bytes "
+                                "(commit fewer sequences or layers per call)", need, kNoAllocScratchBytes);
+  for (int l = 0; l < d->n_layers; ++l) {
+    na.k_layers[l] = d->k_layers[l];
+    na.v_layers[l] = d->v_layers[l];
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(VC_ECUDA, "vc_kv_commit_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: device %d", dev);
+  vc_status st = noalloc_setup(dev, stream);
+  if (st) return st;
+  unsigned char* scratch = g_noalloc_scratch_ptr[dev];
+  KvArgs& a = na.kv;
+  a.block_tables = d->block_tables;
+  a.stride_page = d->stride_page;
+  a.stride_row = d->stride_row;
+  a.stride_head = d->stride_head;
+  a.block_size = paged ? d->block_size : 1;
+  a.max_blocks = d->max_blocks_per_seq;
+  a.n_heads = d->n_kv_heads;
+  a.head_dim = d->head_dim;
+  a.layer_base = d->layer_base;
+  a.paged = paged ? 1 : 0;
+  a.cache_elems = d->cache_elems;
+  a.row_span = row_span;
+  a.err = err_flag_dev ? err_flag_dev : reinterpret_cast<int*>(scratch);
+  a.out.nodes = nullptr;
+  a.out.counters = reinterpret_cast<uint32_t*>(scratch + kNoAllocErrBytes);
+  a.out.croots = scratch + kNoAllocErrBytes + counters_bytes;
+  a.out.roots = kv_roots_dev;
+  a.out.zero_roots = g_noalloc_zero_ptr[dev];
+  // The counters must start at zero; a call that failed part-way may have
+  // left some set, so clear them (and the internal flag) every time.
+  e = cudaMemsetAsync(scratch, 0, kNoAllocErrBytes + counters_bytes, stream);
+  if (e == cudaSuccess) {
+    dim3 grid(chunks, d->n_layers);
+    switch (d->dtype) {
+      case VC_DTYPE_BF16: kv_commit_noalloc_kernel<0><<<grid, kTreeThreads, 0, stream>>>(na); break;
+      case VC_DTYPE_F32: kv_commit_noalloc_kernel<1><<<grid, kTreeThreads, 0, stream>>>(na); break;
+      default: kv_commit_noalloc_kernel<2><<<grid, kTreeThreads, 0, stream>>>(na); break;
+    }
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return set_error(VC_ECUDA, "vc_kv_commit_noalloc launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
+namespace vc {
 
 cudaError_t launch_zero_roots(uint32_t* z, cudaStream_t s) {
   zero_roots_kernel<<<1, 32, 0, s>>>(z);

@@ -92,6 +92,9 @@ cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_
 cudaError_t launch_tagged_hash(int n, int tag, const uint8_t* data, const int64_t* off_dev,
                                int64_t fixed_len, uint8_t* out, cudaStream_t s);
 
+// api.cu: record the calling thread's error text (read by vc_last_error).
+int32_t set_error(int32_t status, const char* fmt, ...);
+
 // int_peak.cu
 cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,
                             double* ops_per_launch);

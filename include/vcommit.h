@@ -133,6 +133,33 @@ typedef struct vc_kv_desc {
 VC_API vc_status vc_kv_commit(vc_ctx* ctx, const vc_kv_desc* desc, uint8_t* kv_roots_dev,
                        vc_tree_set** trees_out);
 
+/*
+ * Allocation-free variant of vc_kv_commit.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory when they commit
+ * (an engine that has reserved all free HBM for its KV cache, or code that
+ * must not stall the device in cudaMalloc).  It calls no cudaMalloc,
+ * cudaFree or allocating library routine and needs no context: its scratch
+ * is a fixed 8 MiB device array inside the library (plus a small padding-root
+ * table), held by every GPU that loads the library until the process exits.
+ *
+ * Same descriptor and output as vc_kv_commit, roots only (no tree set), on
+ * the given stream (NULL = legacy default stream) of the current device.
+ * Limits: at most 64 sequences and 256 layers per call, kv_dim and head_dim
+ * multiples of 8, 16-byte aligned rows (VC_ENOTSUP otherwise), and
+ * 256 + 4 * n_trees (rounded up to 256) + 32 * (sum over trees of
+ * padded_size / 128) bytes of scratch <= 8 MiB (VC_EINVAL otherwise).
+ * err_flag_dev: optional DEVICE int set to 1 when a paged row falls outside
+ * cache_elems (the caller clears it); NULL ignores such rows silently after
+ * zero-hashing them.
+ * The first call on a device looks up the scratch address and fills the
+ * padding-root table, synchronising the stream once: make that first call
+ * before any stream capture.  Every call shares the one scratch array, so
+ * calls whose kernels overlap on the GPU race: serialise them (one stream,
+ * or events).
+ */
+VC_API vc_status vc_kv_commit_noalloc(const vc_kv_desc* desc, uint8_t* kv_roots_dev, int32_t* err_flag_dev,
+                                      void* stream);
+
 /* ----------------------------------------------------------- trace leaves */
 
 /*

@@ -1,19 +1,24 @@
 #!/usr/bin/env python
-"""KV-cache commitment throughput on B200 (trace bytes committed GB/s + kv_roots/s).
+"""Trace-commitment throughput on B200 (trace bytes committed GB/s, + kv_roots/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5] [--impl ours|reference]
 
 A step is one pass of the commitment hot path over one batch of synthetic
-input resident in HBM: every (sequence, layer) K/V tree of the workload is
-hashed (leaf encoding "vi-kv-v1" || layer || pos || f64(K) || f64(V),
-SHA-256) and reduced to its kv_root with all nodes stored for openings; at
-N > 1 the roots are all-gathered (NCCL) and the root-of-roots is built.
+input already resident in HBM.
 
-Workloads (seeded synthetic data, bf16 K/V ~ N(0, 1)):
+KV workloads (bf16 K/V ~ N(0, 1), seeded): every (sequence, layer) tree is
+hashed -- leaf "vi-kv-v1" || u32 layer || u32 pos || f64(K) || f64(V),
+SHA-256 -- and reduced to its kv_root, nodes kept for openings.
   c2  Llama-3.1-8B shape: 32 layers x 8 KV heads x 128, 1 sequence x 4096 tokens (default)
   c3  Qwen2.5-7B shape: 28 layers x 4 x 128, 16 sequences x 8192, paged 16-token blocks, permuted pages
   c5  Llama-3.1-70B shape: 80 layers x 8 x 128, 4 sequences x 32768 per GPU (32 at 8 GPUs)
-Every rank commits its own copy of the workload (weak scaling).
+Retained-state workload:
+  c4  Llama-3.1-8B sampled decode: 256 sequences x 512 steps; per token 32 layers of a_i8[4096] +
+      scale_a + x_attn_i8[4096] + scale_x_attn, and f32 captured logits[128256] ~ N(0, 3^2).
+      A step = retained leaves of all 131 072 tokens, the 256 IO chains, the 512 trace/IO trees,
+      prompt hashes and seed commitments.
+Every rank commits its own copy of the workload (weak scaling); at N > 1 the
+roots are all-gathered (NCCL) and the root-of-roots is built inside the step.
 """
 from __future__ import annotations
 
@@ -29,10 +34,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 BLK_OPS = 1384          # int32 ops per SHA-256 block (one compression), see DESIGN.md
+METRIC = "trace bytes committed GB/s"
 WORKLOADS = {
-    "c2": dict(name="llama3.1-8b-kv", n_layers=32, n_heads=8, head_dim=128, n_seqs=1, seq_len=4096, paged=False),
-    "c3": dict(name="qwen2.5-7b-kv-paged", n_layers=28, n_heads=4, head_dim=128, n_seqs=16, seq_len=8192, paged=True),
-    "c5": dict(name="llama3.1-70b-kv-shard", n_layers=80, n_heads=8, head_dim=128, n_seqs=4, seq_len=32768, paged=False),
+    "c2": dict(kind="kv", name="llama3.1-8b-kv", n_layers=32, n_heads=8, head_dim=128, n_seqs=1, seq_len=4096,
+               paged=False, steps=400),
+    "c3": dict(kind="kv", name="qwen2.5-7b-kv-paged", n_layers=28, n_heads=4, head_dim=128, n_seqs=16,
+               seq_len=8192, paged=True, steps=40),
+    "c4": dict(kind="trace", name="llama3.1-8b-retained-logits", n_layers=32, hidden=4096, n_seqs=256,
+               seq_len=512, vocab=128256, x_attn=True, steps=8),
+    "c5": dict(kind="kv", name="llama3.1-70b-kv-shard", n_layers=80, n_heads=8, head_dim=128, n_seqs=4,
+               seq_len=32768, paged=False, steps=8),
 }
 
 
@@ -40,16 +51,28 @@ def sha_blocks(msg_len: int) -> int:
     return (msg_len + 9 + 63) // 64
 
 
+def tree_blocks(n_leaves: int) -> int:
+    """SHA blocks of build_tree's internal nodes (2 per node, padded size)."""
+    pad = 1 << (n_leaves - 1).bit_length() if n_leaves > 1 else 1
+    return 2 * (pad - 1)
+
+
 def algorithmic(w):
-    """SHA-256 blocks and source bytes of one step (one rank)."""
-    kv = w["n_heads"] * w["head_dim"]
-    leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
-    pad = 1 << (w["seq_len"] - 1).bit_length()
-    nodes = w["n_seqs"] * w["n_layers"] * (pad - 1)
-    blocks = leaves * sha_blocks(16 + 16 * kv) + nodes * 2
-    src_bytes = leaves * kv * 2 * 2
-    msg_bytes = leaves * (16 + 16 * kv)
-    return blocks, src_bytes, msg_bytes, leaves
+    """(SHA blocks of the dominant kernel, other blocks, source bytes, hashed bytes, n_roots) per rank-step."""
+    if w["kind"] == "kv":
+        kv = w["n_heads"] * w["head_dim"]
+        leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
+        blocks = leaves * sha_blocks(16 + 16 * kv) + w["n_seqs"] * w["n_layers"] * tree_blocks(w["seq_len"])
+        return blocks, 0, leaves * kv * 4, leaves * (16 + 16 * kv), w["n_seqs"] * w["n_layers"]
+    L, H, V = w["n_layers"], w["hidden"], w["vocab"]
+    per_layer = H + 4 + 1 + ((H + 4) if w["x_attn"] else 0)
+    base = 14 + L * per_layer
+    logits = 21 + 32 + 4 * V
+    n = w["n_seqs"] * w["seq_len"]
+    leaf_blocks = n * (sha_blocks(base) + sha_blocks(logits))
+    other = n * 2 + 2 * w["n_seqs"] * tree_blocks(w["seq_len"])          # IO chain + trace/IO trees
+    src = n * (L * (H + 4 + ((H + 4) if w["x_attn"] else 0)) + 4 * V)
+    return leaf_blocks, other, src, n * (base + logits), 2 * w["n_seqs"]
 
 
 class Clocks:
@@ -120,6 +143,10 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(pw) if pw else None}
 
 
+# ---------------------------------------------------------------------------
+# KV workloads
+# ---------------------------------------------------------------------------
+
 def make_view(w, device, seed):
     import torch
     from commitllm_b200.commit import KvCacheView
@@ -132,91 +159,285 @@ def make_view(w, device, seed):
         k = [torch.randn(pages, bs, H, D, generator=g, device=f"cuda:{device}", dtype=torch.bfloat16) for _ in range(L)]
         v = [torch.randn(pages, bs, H, D, generator=g, device=f"cuda:{device}", dtype=torch.bfloat16) for _ in range(L)]
         perm = torch.randperm(pages, generator=g, device=f"cuda:{device}").to(torch.int32)
-        bt = perm.view(S, N // bs).contiguous()
-        return KvCacheView(k, v, [N] * S, block_tables=bt)
+        return KvCacheView(k, v, [N] * S, block_tables=perm.view(S, N // bs).contiguous())
     k = [torch.randn(S * N, H, D, generator=g, device=f"cuda:{device}", dtype=torch.bfloat16) for _ in range(L)]
     v = [torch.randn(S * N, H, D, generator=g, device=f"cuda:{device}", dtype=torch.bfloat16) for _ in range(L)]
     return KvCacheView(k, v, [N] * S)
 
 
-def host_transcript(w, seed, n_layers=None):
-    """The workload's K/V as host bf16 bit arrays (numpy), for the CPU legs."""
+class KvStep:
+    """One KV commit of the whole workload (+ the exchange at N > 1)."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import dist as D
+        self.C, self.D, self.torch = C, D, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        self.view = make_view(w, device, seed=1000 + rank)
+        self.n_trees = w["n_seqs"] * w["n_layers"]
+        self.plan = [D.Shard(r, r + 1, 0, self.n_trees) for r in range(world)] if world > 1 else None
+        self.roots = ctx.empty(w["n_seqs"], w["n_layers"], 32)
+        self.ror = ctx.empty(1, 32)
+        self.kernel_events = []
+        self.launches = 1 + (1 if world > 1 else 0)
+
+    def __call__(self, timed: bool):
+        torch, C = self.torch, self.C
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+        roots, trees = C.kv_commit(self.ctx, self.view, keep_trees=True, roots_out=self.roots)
+        if timed:
+            e1.record(self.stream)
+            self.kernel_events.append((e0, e1))
+        if self.world > 1:
+            with torch.cuda.stream(self.stream):
+                full = self.D.gather_roots(roots.view(-1, 32), self.plan, self.world, self.n_trees)
+                C.build_trees(self.ctx, full.view(-1, 32), [0, self.world * self.n_trees], keep_trees=False,
+                              roots_out=self.ror)
+        trees.free()
+
+    def host_inputs(self):
+        return list(self.view.k_layers) + list(self.view.v_layers)
+
+    def e2e_step(self, dev_tensors, roots_host):
+        C = self.C
+        L = self.w["n_layers"]
+        view = C.KvCacheView(dev_tensors[:L], dev_tensors[L:], self.view.seq_lens,
+                             block_tables=self.view.block_tables)
+        roots, trees = C.kv_commit(self.ctx, view, keep_trees=True, roots_out=self.roots)
+        roots_host.copy_(roots.view(-1), non_blocking=True)
+        trees.free()
+        return roots.numel()
+
+
+# ---------------------------------------------------------------------------
+# Retained-state workload (c4)
+# ---------------------------------------------------------------------------
+
+class TraceStep:
+    """Retained leaves + IO chains + trace/IO trees + prompt/seed hashes of n_seqs requests."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import dist as D
+        self.C, self.D, self.torch = C, D, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        dev = f"cuda:{device}"
+        g = torch.Generator(device=dev)
+        g.manual_seed(2000 + rank)
+        L, H, B, T, V = w["n_layers"], w["hidden"], w["n_seqs"], w["seq_len"], w["vocab"]
+        # captures as a decode engine lays them out: step k, layer l, batch row = sequence
+        self.a = torch.randint(-128, 128, (T, L, B, H), generator=g, device=dev, dtype=torch.int8)
+        self.x = torch.randint(-128, 128, (T, L, B, H), generator=g, device=dev, dtype=torch.int8) if w["x_attn"] else None
+        self.sa = torch.rand(T, L, B, generator=g, device=dev) * 0.05 + 1e-3
+        self.sx = torch.rand(T, L, B, generator=g, device=dev) * 0.05 + 1e-3
+        self.logits = torch.randn(B * T, V, generator=g, device=dev) * 3.0       # row = token s*T + k
+        self.tok = torch.randint(0, V, (B * T,), generator=g, device=dev, dtype=torch.int32)
+        self.seeds = torch.randint(0, 256, (B, 32), generator=g, device=dev, dtype=torch.uint8)
+        self.prompts = [f"synthetic prompt {rank}:{s}".encode() for s in range(B)]
+        self.n = B * T
+        self.plan = self.make_plan()
+        self.both = ctx.empty(2 * self.n, 32)
+        self.tree_off = [s * T for s in range(B)] + [self.n + s * T for s in range(B + 1)]
+        self.roots = ctx.empty(2 * B, 32)
+        self.n_roots = 2 * B
+        self.rplan = [D.Shard(r, r + 1, 0, self.n_roots) for r in range(world)] if world > 1 else None
+        self.ror = ctx.empty(1, 32)
+        self.kernel_events = []
+        self.launches = 5 + (1 if world > 1 else 0)
+
+    def make_plan(self, a=None, x=None, sa=None, sx=None, logits=None):
+        import numpy as np
+        C, w = self.C, self.w
+        a = self.a if a is None else a
+        x = self.x if x is None else x
+        sa = self.sa if sa is None else sa
+        sx = self.sx if sx is None else sx
+        logits = self.logits if logits is None else logits
+        L, H, B, T = w["n_layers"], w["hidden"], w["n_seqs"], w["seq_len"]
+        t = np.arange(B * T)
+        lay = C.TraceLayout(
+            n_layers=L, hidden=H, fwd_rows=[B] * T, tok_fwd=t % T, tok_row=t // T,
+            a_rows=[[a.data_ptr() + ((k * L + l) * B) * H for l in range(L)] for k in range(T)],
+            scale_a=[[sa.data_ptr() + 4 * ((k * L + l) * B) for l in range(L)] for k in range(T)], scale_stride=1,
+            x_attn_rows=None if x is None else [[x.data_ptr() + ((k * L + l) * B) * H for l in range(L)] for k in range(T)],
+            scale_x_attn=None if x is None else [[sx.data_ptr() + 4 * ((k * L + l) * B) for l in range(L)] for k in range(T)],
+            scale_x_stride=1, logits=logits, tok_logits_row=t)
+        return C.TracePlan(lay)
+
+    def __call__(self, timed: bool, plan=None, tok=None, seeds=None):
+        torch, C = self.torch, self.C
+        plan = self.plan if plan is None else plan
+        n = self.n
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+        plan.run(self.ctx, self.both[:n])
+        if timed:
+            e1.record(self.stream)
+            self.kernel_events.append((e0, e1))
+        ph = C.prompt_hashes(self.ctx, self.prompts)
+        C.io_chain(self.ctx, self.both[:n], self.tok if tok is None else tok, ph,
+                   [s * self.w["seq_len"] for s in range(self.w["n_seqs"] + 1)], out=self.both[n:])
+        C.build_trees(self.ctx, self.both, self.tree_off, keep_trees=False, roots_out=self.roots)
+        C.seed_commitments(self.ctx, self.seeds if seeds is None else seeds)
+        if self.world > 1:
+            with torch.cuda.stream(self.stream):
+                full = self.D.gather_roots(self.roots, self.rplan, self.world, self.n_roots)
+                C.build_trees(self.ctx, full.view(-1, 32), [0, self.world * self.n_roots], keep_trees=False,
+                              roots_out=self.ror)
+
+    def host_inputs(self):
+        out = [self.a, self.sa, self.sx, self.logits, self.tok, self.seeds]
+        if self.x is not None:
+            out.insert(1, self.x)
+        return out
+
+    def e2e_step(self, dev_tensors, roots_host):
+        if self.x is not None:
+            a, x, sa, sx, logits, tok, seeds = dev_tensors
+        else:
+            a, sa, sx, logits, tok, seeds = dev_tensors
+            x = None
+        key = tuple(t.data_ptr() for t in dev_tensors)
+        if getattr(self, "_e2e_key", None) != key:
+            self._e2e_plan = self.make_plan(a, x, sa, sx, logits)
+            self._e2e_key = key
+        self(False, plan=self._e2e_plan, tok=tok, seeds=seeds)
+        roots_host.copy_(self.roots.view(-1), non_blocking=True)
+        return self.roots.numel()
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle's C restatement of the reference algorithm
+# ---------------------------------------------------------------------------
+
+def host_kv(w, seed, n_layers):
     import numpy as np
     from tests import synth
-    L = w["n_layers"] if n_layers is None else n_layers
     rows = w["n_seqs"] * w["seq_len"]
     rng = np.random.default_rng(seed)
-    shape = (L, rows, w["n_heads"], w["head_dim"])
-    k = synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))
-    v = synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))
-    return k, v
+    shape = (n_layers, rows, w["n_heads"], w["head_dim"])
+    return (synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)),
+            synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)))
 
 
-def cpu_commit_seconds(w, n_layers, n_threads, seed=7):
-    """Time the oracle's C restatement (reference algorithm) on n_layers of the workload."""
-    import numpy as np
+def cpu_kv(w, n_layers, n_threads, reps=1, seed=7):
+    """Seconds per commit of n_layers of the KV workload (median of reps), reference algorithm."""
     from commitllm_b200._lib import VC_DTYPE_BF16
     from tests.kvref import Transcript
-    k, v = host_transcript(w, seed, n_layers)
+    k, v = host_kv(w, seed, n_layers)
     tr = Transcript(k, v, [w["seq_len"]] * w["n_seqs"], VC_DTYPE_BF16)
-    t0 = time.perf_counter()
-    tr.oracle(n_threads=n_threads, with_nodes=True)
-    return time.perf_counter() - t0
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        tr.oracle(n_threads=n_threads, with_nodes=True)
+        ts.append(time.perf_counter() - t0)
+    return sorted(ts)[len(ts) // 2]
 
 
-def cpu_baseline_leg(w, reference_threads=False, budget_s=20.0):
-    """(value GB/s, cores, sample text) of the CPU restatement on a bounded sample."""
+def cpu_trace(w, n_tokens, n_threads, reps=1, seed=9):
+    """Seconds to hash n_tokens retained leaves (+ their IO chain) of the c4 workload on the host."""
+    import ctypes
+    import numpy as np
+    from commitllm_b200._lib import TraceDesc
+    from oracle import vco
+    L, H, V = w["n_layers"], w["hidden"], w["vocab"]
+    rng = np.random.default_rng(seed)
+    a = rng.integers(-128, 128, size=(L, n_tokens, H), dtype=np.int8)
+    x = rng.integers(-128, 128, size=(L, n_tokens, H), dtype=np.int8)
+    sc = rng.random((L, n_tokens), dtype=np.float32)
+    logits = rng.standard_normal((n_tokens, V), dtype=np.float32)
+    keep = [a, x, sc, logits]
+
+    def per_layer(arr, stride):
+        p = (ctypes.c_void_p * L)(*[arr.ctypes.data + l * stride for l in range(L)])
+        keep.append(p)
+        return ctypes.cast(p, ctypes.POINTER(ctypes.c_void_p))
+
+    def i32(vals):
+        arr = (ctypes.c_int32 * len(vals))(*vals)
+        keep.append(arr)
+        return ctypes.cast(arr, ctypes.POINTER(ctypes.c_int32))
+
+    d = TraceDesc()
+    d.n_tokens, d.n_layers, d.hidden, d.n_fwd = n_tokens, L, H, 1
+    d.fwd_rows, d.tok_fwd, d.tok_row = i32([n_tokens]), i32([0] * n_tokens), i32(list(range(n_tokens)))
+    d.a_rows = per_layer(a, n_tokens * H)        # layer l, row r at a + l*n*H + r*H
+    d.scale_a = per_layer(sc, n_tokens * 4)
+    d.scale_stride = 1
+    if w["x_attn"]:
+        d.x_attn_rows = per_layer(x, n_tokens * H)
+        d.scale_x_attn = per_layer(sc, n_tokens * 4)
+        d.scale_x_stride = 1
+    d.logits, d.vocab, d.logits_rows, d.logits_stride = logits.ctypes.data, V, n_tokens, V
+    d.tok_logits_row = i32(list(range(n_tokens)))
+    leaves = np.zeros((n_tokens, 32), np.uint8)
+    toks = rng.integers(0, V, size=n_tokens, dtype=np.uint32)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        vco.lib().vco_trace_leaves(ctypes.byref(d), leaves.ctypes.data, n_threads)
+        vco.io_chain(leaves, toks, b"synthetic prompt")
+        ts.append(time.perf_counter() - t0)
+    return sorted(ts)[len(ts) // 2]
+
+
+def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
+    """(GB/s, threads, sample text, seconds) of the CPU restatement on a bounded sample of w."""
     ncpu = os.cpu_count() or 1
-    if reference_threads:
-        threads = 1  # the reference hashes KV trees in a sequential per-layer loop
-    else:
-        threads = max(1, min(ncpu, w["n_seqs"] * w["n_layers"]))
-    # size the sample: start with a few layers and grow within the budget
-    layers = max(1, min(w["n_layers"], threads))
-    dt = cpu_commit_seconds(w, layers, threads)
-    per_layer = dt / layers
-    more = int(min(w["n_layers"], max(layers, (budget_s * 0.5) / max(per_layer, 1e-6))))
-    if more > layers and more * per_layer < budget_s:
-        layers = more
-        dt = cpu_commit_seconds(w, layers, threads)
-    _, src, _, _ = algorithmic(dict(w, n_layers=layers))
-    return src / dt / 1e9, threads, layers, dt
+    _, _, src_full, _, _ = algorithmic(w)
+    if w["kind"] == "kv":
+        # the reference hashes KV trees in a sequential per-layer loop (prover/src/lib.rs:454-478)
+        threads = 1 if reference_threads else max(1, min(ncpu, w["n_seqs"] * w["n_layers"]))
+        layers = max(1, min(w["n_layers"], threads))
+        per = cpu_kv(w, layers, threads) / layers
+        layers = int(min(w["n_layers"], max(layers, budget_s * 0.5 / max(per, 1e-6))))
+        dt = cpu_kv(w, layers, threads, reps=reps)
+        src = src_full * layers / w["n_layers"]
+        sample = (f"{layers} of {w['n_layers']} layers x {w['n_seqs']} seq x {w['seq_len']} tokens, oracle C "
+                  f"restatement (OpenSSL SHA-256), {threads} thread(s) over trees")
+        return src / dt / 1e9, threads, sample, dt
+    # retained leaves: the reference uses rayon over tokens (prover/src/lib.rs:371-393), IO chain serial
+    threads = ncpu
+    n_tok = 32 * threads
+    dt = cpu_trace(w, n_tok, threads)
+    n_tok = int(min(4096, max(n_tok, n_tok * budget_s * 0.5 / max(dt, 1e-6))))   # <= ~3.2 GB of host data
+    dt = cpu_trace(w, n_tok, threads, reps=reps)
+    per_tok = src_full / (w["n_seqs"] * w["seq_len"])
+    sample = (f"{n_tok} of {w['n_seqs'] * w['seq_len']} tokens (retained leaves with x_attn + logits wrap, "
+              f"IO chain), oracle C restatement (OpenSSL SHA-256), {threads} threads over tokens")
+    return per_tok * n_tok / dt / 1e9, threads, sample, dt
+
+
+def config_of(w, world):
+    c = {k: v for k, v in w.items() if k not in ("steps", "name", "kind")}
+    c["workload"] = w["name"]
+    c["parallelism"] = f"shard-by-sequence x{world}"
+    return c
 
 
 def run_reference(args, w, rank, world):
     """The reference's CPU algorithm (oracle port, all host threads) on bounded samples."""
     if rank != 0:
         return
-    from commitllm_b200._lib import VC_DTYPE_BF16
-    from tests.kvref import Transcript
-    ncpu = os.cpu_count() or 1
-    threads = max(1, min(ncpu, w["n_seqs"] * w["n_layers"]))
-    layers = max(1, min(w["n_layers"], threads))
-    k, v = host_transcript(w, 7, layers)
-    tr = Transcript(k, v, [w["seq_len"]] * w["n_seqs"], VC_DTYPE_BF16)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        tr.oracle(n_threads=threads, with_nodes=True)
-        if i >= args.warmup:
-            vals.append(time.perf_counter() - t0)
-    t = sorted(vals)[len(vals) // 2]
-    _, src, _, leaves = algorithmic(dict(w, n_layers=layers))
-    value = src / t / 1e9
-    sample = (f"{layers} of {w['n_layers']} layers x {w['n_seqs']} seq x {w['seq_len']} tokens per step, "
-              f"oracle C restatement (OpenSSL SHA-256), {threads} threads over trees, median of {len(vals)} steps")
+    reps = max(1, args.steps)
+    val, threads, sample, dt = cpu_leg(w, reference_threads=False, reps=reps)
     line = {
-        "impl": "reference", "metric": "trace bytes committed GB/s", "value": round(value, 4), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": w["name"], "layers": w["n_layers"], "kv_heads": w["n_heads"], "head_dim": w["head_dim"],
-                   "seqs": w["n_seqs"], "seq_len": w["seq_len"], "paged": w["paged"]},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "kv_roots_per_s": round(w["n_seqs"] * layers / t, 3),
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": config_of(w, world),
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample + f", median of {reps} steps"},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
+
+# ---------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser()
@@ -227,12 +448,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--seqs", type=int, default=None, help="override the workload's sequence count")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.seqs:
+        w["n_seqs"] = args.seqs
     if args.steps is None:
         # about a second of timed work, so the clock sampler sees the region
-        args.steps = {"c2": 400, "c3": 40, "c5": 8}[args.workload] if args.impl == "ours" else 10
+        args.steps = w["steps"] if args.impl == "ours" else 5
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -245,7 +469,6 @@ def main():
     import torch
     import torch.distributed as dist
     from commitllm_b200 import commit as C
-    from commitllm_b200 import dist as D
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -253,32 +476,9 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     stream = torch.cuda.Stream(local)
     ctx = C.Context(local, stream)
-    view = make_view(w, local, seed=1000 + rank)
+    step = (KvStep if w["kind"] == "kv" else TraceStep)(w, ctx, stream, local, rank, world)
     torch.cuda.synchronize()
-    blocks, src_bytes, msg_bytes, leaves = algorithmic(w)
-    n_trees = w["n_seqs"] * w["n_layers"]
-    # weak scaling: rank r holds all trees of its own copy of the workload
-    plan = [D.Shard(r, r + 1, 0, n_trees) for r in range(world)] if world > 1 else None
-
-    roots_buf = ctx.empty(w["n_seqs"], w["n_layers"], 32)
-    ror_buf = ctx.empty(1, 32)
-    kern_ms = []
-
-    def step(timed):
-        e0 = e1 = None
-        if timed:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        roots, trees = C.kv_commit(ctx, view, keep_trees=True, roots_out=roots_buf)
-        if timed:
-            e1.record(stream)
-            kern_ms.append((e0, e1))
-        if world > 1:
-            with torch.cuda.stream(stream):
-                full = D.gather_roots(roots.view(-1, 32), plan, world, n_trees, group=None)
-                C.build_trees(ctx, full.view(-1, 32), [0, world * n_trees], keep_trees=False, roots_out=ror_buf)
-        trees.free()
+    blocks, other_blocks, src_bytes, msg_bytes, n_roots = algorithmic(w)
 
     for _ in range(args.warmup):
         step(False)
@@ -286,6 +486,7 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    step.kernel_events.clear()
 
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -306,7 +507,7 @@ def main():
         total_ms = float(tt.item())
         dist.barrier()
     ms_step = total_ms / args.steps
-    kms = sorted(a.elapsed_time(b) for a, b in kern_ms)
+    kms = [a.elapsed_time(b) for a, b in step.kernel_events]
     k_avg = sum(kms) / len(kms)
 
     # integer-ALU peak probe on the same GPU, same run
@@ -316,31 +517,43 @@ def main():
     # end to end through the public API from pinned host memory
     e2e = None
     if not args.no_e2e:
-        host_k = [t.cpu().pin_memory() for t in view.k_layers]
-        host_v = [t.cpu().pin_memory() for t in view.v_layers]
-        dev_k = [torch.empty_like(t) for t in view.k_layers]
-        dev_v = [torch.empty_like(t) for t in view.v_layers]
-        view2 = C.KvCacheView(dev_k, dev_v, view.seq_lens, block_tables=view.block_tables)
-        roots_host = torch.empty(w["n_seqs"], w["n_layers"], 32, dtype=torch.uint8).pin_memory()
-        h2d = sum(t.numel() * t.element_size() for t in host_k + host_v)
+        e2e_note = None
+        estep, e_src, e_roots = step, src_bytes, n_roots
+        if w["kind"] == "trace":
+            # 101.6 GB of captures per step would not fit pinned host memory: the
+            # e2e leg commits a 16-sequence slice of the same workload
+            w_e = dict(w, n_seqs=16)
+            estep = TraceStep(w_e, ctx, stream, local, rank, world=1)
+            _, _, e_src, _, e_roots = algorithmic(w_e)
+            e2e_note = "16 of 256 sequences per step (same shapes)"
+        elif src_bytes > (4 << 30):
+            # keep the pinned host copy bounded: commit a layer slice of the same workload
+            n_l = max(1, int(w["n_layers"] * (4 << 30) // src_bytes))
+            w_e = dict(w, n_layers=n_l)
+            estep = KvStep(w_e, ctx, stream, local, rank, world=1)
+            _, _, e_src, _, e_roots = algorithmic(w_e)
+            e2e_note = f"{n_l} of {w['n_layers']} layers per step (same shapes)"
+        host = [t.cpu().pin_memory() for t in estep.host_inputs()]
+        dev = [torch.empty_like(t) for t in estep.host_inputs()]
+        roots_host = torch.empty(e_roots * 32, dtype=torch.uint8).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in host)
 
         def e2e_step():
             with torch.cuda.stream(stream):
-                for d, h in zip(dev_k + dev_v, host_k + host_v):
+                for d, h in zip(dev, host):
                     d.copy_(h, non_blocking=True)
-                roots, trees = C.kv_commit(ctx, view2, keep_trees=True, roots_out=roots_buf)
-                roots_host.copy_(roots, non_blocking=True)
-                trees.free()
+                return estep.e2e_step(dev, roots_host)
 
-        for _ in range(3):
+        for _ in range(3 if w["kind"] == "kv" else 1):
             e2e_step()
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
-        n_e2e = max(3, min(args.steps, 10))
+        n_e2e = max(3, min(args.steps, 10)) if w["kind"] == "kv" else 2
+        d2h = 0
         a.record(stream)
         for _ in range(n_e2e):
-            e2e_step()
+            d2h = e2e_step()
         b.record(stream)
         torch.cuda.synchronize()
         e_ms = a.elapsed_time(b) / n_e2e
@@ -348,18 +561,17 @@ def main():
             tt = torch.tensor([e_ms], device=f"cuda:{local}")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e_ms = float(tt.item())
-        e2e = {"value": round(src_bytes * world / (e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": w["n_seqs"] * w["n_layers"] * 32,
-               "ms_per_step": round(e_ms, 3)}
-        del host_k, host_v, dev_k, dev_v
+        e2e = {"value": round(e_src * world / (e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e_ms, 3)}
+        if e2e_note:
+            e2e["sample"] = e2e_note
+        del host, dev, estep
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        val, cores, layers, dt = cpu_baseline_leg(w, reference_threads=True)
+        val, cores, sample, dt = cpu_leg(w, reference_threads=True)
         cpu = {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"{layers} of {w['n_layers']} layers x {w['n_seqs']} seq x {w['seq_len']} tokens "
-                         f"({dt:.2f} s), oracle C restatement with OpenSSL SHA-256, the reference's sequential "
-                         f"per-layer KV-tree loop (1 thread)"}
+               "sample": sample + f" ({dt:.2f} s); the reference's own threading for this path"}
 
     if world > 1:
         dist.destroy_process_group()
@@ -374,29 +586,27 @@ def main():
     alu_achieved = blocks * BLK_OPS / (k_avg * 1e-3) / 1e12
     alu_peak = peak_ops / 1e12
     hbm_achieved = src_bytes / (k_avg * 1e-3) / 1e9
-    clocks = clk.summary()
-    value = src_bytes * world / (ms_step * 1e-3) / 1e9
     line = {
-        "metric": "trace bytes committed GB/s", "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": w["name"], "layers": w["n_layers"], "kv_heads": w["n_heads"],
-                   "head_dim": w["head_dim"], "seqs_per_gpu": w["n_seqs"], "seq_len": w["seq_len"],
-                   "paged": w["paged"], "parallelism": f"shard-by-sequence x{world}",
-                   "l2": "inputs larger than L2 (%.0f MB per GPU)" % (src_bytes / 1e6)},
-        "kv_roots_per_s": round(n_trees * world / (ms_step * 1e-3), 2),
+        "metric": METRIC, "value": round(src_bytes * world / (ms_step * 1e-3) / 1e9, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": dict(config_of(w, world), l2="inputs larger than L2 (%.0f MB per GPU)" % (src_bytes / 1e6)),
+        "roots_per_s": round(n_roots * world / (ms_step * 1e-3), 2),
         "hashed_msg_GBps": round(msg_bytes * world / (ms_step * 1e-3) / 1e9, 3),
         "roofline": {"bound": "int_alu", "achieved": round(alu_achieved, 3), "peak": round(alu_peak, 3),
                      "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4), "traffic": None,
+                     "kernel": "kv_commit_kernel" if w["kind"] == "kv" else "trace_leaf_kernel",
                      "kernel_ms": round(k_avg, 4), "sha_blocks": blocks, "ops_per_block": BLK_OPS,
                      "peak_source": "vc_int_peak SHA-mix probe, this GPU, this run",
                      "hbm": {"achieved": round(hbm_achieved, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(hbm_achieved / hbm, 4), "peak_source": "MEASURED_PEAKS.json hbm_gbs"}},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * (1 + (1 if world > 1 else 0)),
-        "clocks": clocks,
+        "gpu_launches": args.steps * step.launches,
+        "clocks": clk.summary(),
     }
+    if w["kind"] == "kv":
+        line["kv_roots_per_s"] = line["roots_per_s"]
     print(json.dumps(line), flush=True)
 
 

@@ -359,57 +359,69 @@ class TraceLayout:
     tok_logits_row: Optional[Sequence[int]] = None
 
 
+class TracePlan:
+    """A ``vc_trace_desc`` built once from a :class:`TraceLayout`, for repeated commits."""
+
+    def __init__(self, lay: TraceLayout):
+        self.n = len(lay.tok_fwd)
+        d = TraceDesc()
+        keep = []
+        d.n_tokens = self.n
+        d.n_layers = lay.n_layers
+        d.hidden = lay.hidden
+        d.n_fwd = len(lay.fwd_rows)
+
+        def arr32(x):
+            a = np.ascontiguousarray(np.asarray(x, dtype=np.int32))
+            keep.append(a)
+            return a.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+
+        def arrp(rows):
+            a = np.ascontiguousarray(np.asarray(rows, dtype=np.uint64).reshape(-1))
+            keep.append(a)
+            return ctypes.cast(a.ctypes.data, ctypes.POINTER(ctypes.c_void_p))
+
+        d.fwd_rows = arr32(lay.fwd_rows)
+        d.tok_fwd = arr32(lay.tok_fwd)
+        d.tok_row = arr32(lay.tok_row)
+        d.a_rows = arrp(lay.a_rows)
+        d.scale_a = arrp(lay.scale_a)
+        d.scale_stride = int(lay.scale_stride)
+        if lay.x_attn_rows is not None:
+            d.x_attn_rows = arrp(lay.x_attn_rows)
+            d.scale_x_attn = arrp(lay.scale_x_attn)
+            d.scale_x_stride = int(lay.scale_x_stride)
+        for name, ten, rows, esz in (("fr", lay.final_residual, lay.tok_fr_row, 4),
+                                     ("lp", lay.lp_hidden, lay.tok_lp_row, 2),
+                                     ("logits", lay.logits, lay.tok_logits_row, 4)):
+            if ten is None:
+                continue
+            _require_cuda(ten, name)
+            if ten.element_size() != esz or ten.dim() != 2 or ten.stride(1) != 1:
+                raise ValueError(f"{name} must be a 2-D row-major tensor of {esz}-byte elements")
+            ptr, dim, nrows, stride = ten.data_ptr(), ten.shape[1], ten.shape[0], ten.stride(0)
+            if name == "fr":
+                d.final_residual, d.fr_dim, d.fr_rows, d.fr_stride, d.tok_fr_row = ptr, dim, nrows, stride, arr32(rows)
+            elif name == "lp":
+                d.lp_hidden, d.lp_dim, d.lp_rows, d.lp_stride, d.tok_lp_row = ptr, dim, nrows, stride, arr32(rows)
+            else:
+                d.logits, d.vocab, d.logits_rows, d.logits_stride, d.tok_logits_row = ptr, dim, nrows, stride, arr32(rows)
+        self.desc = d
+        self._keep = keep
+
+    def run(self, ctx: Context, out: torch.Tensor) -> torch.Tensor:
+        if out.shape[0] < self.n or not out.is_contiguous():
+            raise ValueError("out must be a contiguous [n_tokens, 32] uint8 CUDA tensor")
+        check(lib().vc_trace_leaves(ctx.handle, ctypes.byref(self.desc), ctypes.c_void_p(out.data_ptr())))
+        return out[: self.n]
+
+
 def trace_leaves(ctx: Context, lay: TraceLayout, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Retained-state leaves of every token, ``[n_tokens, 32]`` on the device."""
-    n = len(lay.tok_fwd)
+    plan = TracePlan(lay)
     if out is None:
-        out = ctx.empty(max(n, 1), 32)
-    d = TraceDesc()
-    keep = []
-    d.n_tokens = n
-    d.n_layers = lay.n_layers
-    d.hidden = lay.hidden
-    d.n_fwd = len(lay.fwd_rows)
-
-    def arr32(x):
-        a = _i32(x)
-        keep.append(a)
-        return ctypes.cast(a, ctypes.POINTER(ctypes.c_int32))
-
-    def arrp(rows):
-        flat = [p for r in rows for p in r]
-        a = _ptrs(flat)
-        keep.append(a)
-        return ctypes.cast(a, ctypes.POINTER(ctypes.c_void_p))
-
-    d.fwd_rows = arr32(lay.fwd_rows)
-    d.tok_fwd = arr32(lay.tok_fwd)
-    d.tok_row = arr32(lay.tok_row)
-    d.a_rows = arrp(lay.a_rows)
-    d.scale_a = arrp(lay.scale_a)
-    d.scale_stride = int(lay.scale_stride)
-    if lay.x_attn_rows is not None:
-        d.x_attn_rows = arrp(lay.x_attn_rows)
-        d.scale_x_attn = arrp(lay.scale_x_attn)
-        d.scale_x_stride = int(lay.scale_x_stride)
-    for name, ten, rows, esz in (("fr", lay.final_residual, lay.tok_fr_row, 4),
-                                 ("lp", lay.lp_hidden, lay.tok_lp_row, 2),
-                                 ("logits", lay.logits, lay.tok_logits_row, 4)):
-        if ten is None:
-            continue
-        _require_cuda(ten, name)
-        if ten.element_size() != esz or ten.dim() != 2 or ten.stride(1) != 1:
-            raise ValueError(f"{name} must be a 2-D row-major tensor of {esz}-byte elements")
-        ptr, dim, nrows, stride = ten.data_ptr(), ten.shape[1], ten.shape[0], ten.stride(0)
-        if name == "fr":
-            d.final_residual, d.fr_dim, d.fr_rows, d.fr_stride, d.tok_fr_row = ptr, dim, nrows, stride, arr32(rows)
-        elif name == "lp":
-            d.lp_hidden, d.lp_dim, d.lp_rows, d.lp_stride, d.tok_lp_row = ptr, dim, nrows, stride, arr32(rows)
-        else:
-            d.logits, d.vocab, d.logits_rows, d.logits_stride, d.tok_logits_row = ptr, dim, nrows, stride, arr32(rows)
-    check(lib().vc_trace_leaves(ctx.handle, ctypes.byref(d), ctypes.c_void_p(out.data_ptr())))
-    del keep
-    return out[:n]
+        out = ctx.empty(max(plan.n, 1), 32)
+    return plan.run(ctx, out)
 
 
 def int_peak(ctx: Context, variant: int = 0, iters: int = 20000) -> float:

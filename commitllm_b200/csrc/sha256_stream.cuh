@@ -2,10 +2,13 @@
 // byte offsets (the retained-state leaf of merkle.rs:144-161 has 4101-byte
 // layer records, so its a_i8 rows start at every alignment mod 4).
 //
-// The 16-word block buffer lives in shared memory, word-major across the CTA
-// (word k of thread tid at buf[k * NT]), so every access of a warp is one
-// conflict-free wavefront.  All threads of a warp hash messages of the same
-// layout, so the fill position -- and every branch on it -- is warp-uniform.
+// Whole blocks inside a field are assembled straight from global memory in
+// registers (4-byte loads, one byte-permute per word realigns and byte-swaps).
+// The partial blocks where fields meet go through a 16-word block buffer in
+// shared memory, word-major across the CTA (word k of thread tid at
+// buf[k * NT]), so every access of a warp is one conflict-free wavefront.
+// All threads of a warp hash messages of the same layout, so the fill
+// position -- and every branch on it -- is warp-uniform.
 #pragma once
 #include "sha256_core.cuh"
 
@@ -80,8 +83,62 @@ struct Sha256Stream {
     for (int i = 0; i < 8; ++i) put_be(d[i]);
   }
 
-  // Append len bytes from p (any alignment).
+  // Append len bytes from p (any alignment).  Whole blocks inside the field
+  // are assembled in registers; only the partial blocks at its ends go
+  // through the shared-memory buffer.
   __device__ __forceinline__ void put_array(const uint8_t* p, int64_t len) {
+    // head: up to the next block boundary of the message
+    if (fill != 0) {
+      const int64_t head = 64 - fill;
+      if (len <= head + 68) {
+        put_array_buffered(p, len);
+        return;
+      }
+      put_array_buffered(p, head);
+      p += head;
+      len -= head;
+    }
+    // interior: the buffer is empty here; keep 4 bytes of margin so the
+    // last word load of a misaligned block stays inside the field
+    const int64_t nblk = len >= 68 ? (len - 4) >> 6 : 0;
+    if (nblk > 0) {
+      direct_blocks(p, nblk);
+      p += nblk * 64;
+      len -= nblk * 64;
+      total += uint64_t(nblk) * 64;
+    }
+    if (len > 0) put_array_buffered(p, len);
+  }
+
+  // nblk whole 64-byte blocks from p (any alignment), straight from global
+  // memory into the compression, one block of prefetch.  The buffer must be
+  // empty (fill == 0).  Reads bytes [p & ~3, p + 64 * nblk + 3).
+  __device__ __forceinline__ void direct_blocks(const uint8_t* p, int64_t nblk) {
+    const uint32_t s = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3u);
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(p - s);
+    // message word j = bytes s..s+3 of (x[j], x[j+1]), most significant first
+    const uint32_t sel = (s << 12) | ((s + 1) << 8) | ((s + 2) << 4) | (s + 3);
+    uint32_t x[17];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = __ldg(q + j);
+    x[16] = s ? __ldg(q + 16) : 0u;
+    for (int64_t b = 0; b < nblk; ++b) {
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = __byte_perm(x[j], x[j + 1], sel);
+      if (b + 1 < nblk) {
+        // the next block's loads are in flight during this compression
+        const uint32_t* qn = q + 16 * (b + 1);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] = __ldg(qn + j);
+        x[16] = s ? __ldg(qn + 16) : 0u;
+      }
+      compress(h, w);
+    }
+  }
+
+  // Append len bytes from p through the shared-memory block buffer.
+  __device__ __forceinline__ void put_array_buffered(const uint8_t* p, int64_t len) {
     while (len > 0 && (reinterpret_cast<uintptr_t>(p) & 3u) != 0) {
       put_byte(__ldg(p));
       ++p;

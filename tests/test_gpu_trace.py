@@ -256,3 +256,33 @@ def test_verilm_rs_argument_errors(ctx):
     with pytest.raises(NotImplementedError):
         V.commit_minimal_from_captures([b"\0" * 4], np.zeros(4, np.float32), 1, [1], [1], b"p", b"\0" * 32,
                                        manifest={"x": 1}, ctx=ctx)
+
+
+def test_c4_shape_retained_leaves_through_trace_plan(ctx):
+    """Full-width sampled-decode leaves (32 layers x 4096 a_i8 + x_attn, 128 256 f32 logits)
+    laid out as the benchmark lays them ([step, layer, batch, hidden]), vs the oracle."""
+    L, H, B, T, V = 32, 4096, 3, 4, 128256
+    a = synth.activations_i8(61, (T, L, B, H))
+    x = synth.activations_i8(62, (T, L, B, H))
+    sa = synth.scales_f32(63, T * L * B).reshape(T, L, B)
+    sx = synth.scales_f32(64, T * L * B).reshape(T, L, B)
+    logits = synth.logits_f32(65, (B * T, V))
+    ad, xd, sad, sxd, ld = (ctx.to_device(v) for v in (a, x, sa, sx, logits))
+    t = np.arange(B * T)
+    lay = C.TraceLayout(
+        n_layers=L, hidden=H, fwd_rows=[B] * T, tok_fwd=t % T, tok_row=t // T,
+        a_rows=[[ad.data_ptr() + ((k * L + l) * B) * H for l in range(L)] for k in range(T)],
+        scale_a=[[sad.data_ptr() + 4 * ((k * L + l) * B) for l in range(L)] for k in range(T)], scale_stride=1,
+        x_attn_rows=[[xd.data_ptr() + ((k * L + l) * B) * H for l in range(L)] for k in range(T)],
+        scale_x_attn=[[sxd.data_ptr() + 4 * ((k * L + l) * B) for l in range(L)] for k in range(T)],
+        scale_x_stride=1, logits=ld, tok_logits_row=t)
+    plan = C.TracePlan(lay)
+    out = ctx.empty(B * T, 32)
+    plan.run(ctx, out)
+    ctx.sync(timeout_ms=60000)
+    got = [bytes(v) for v in out.cpu().numpy()]
+    for i in range(B * T):
+        s, k = i // T, i % T
+        layers = [O.RetainedLayerState(a[k, l, s].tobytes(), float(sa[k, l, s]), x[k, l, s].tobytes(),
+                                       float(sx[k, l, s])) for l in range(L)]
+        assert got[i] == O.hash_retained_with_captured_logits(layers, None, None, logits[i])

@@ -510,6 +510,36 @@ def main():
     kms = [a.elapsed_time(b) for a, b in step.kernel_events]
     k_avg = sum(kms) / len(kms)
 
+    # the token-level IO chain of the KV workloads' sequences, timed on its own
+    # (serial: one warp per sequence; not part of the KV step above)
+    io_chain = None
+    if w["kind"] == "kv":
+        S, T = w["n_seqs"], w["seq_len"]
+        g = torch.Generator(device=f"cuda:{local}")
+        g.manual_seed(77)
+        leaves = torch.randint(0, 256, (S * T, 32), generator=g, device=f"cuda:{local}", dtype=torch.uint8)
+        tok = torch.randint(0, 128256, (S * T,), generator=g, device=f"cuda:{local}", dtype=torch.int32)
+        ph = C.prompt_hashes(ctx, [b"synthetic prompt %d" % s for s in range(S)])
+        io_out = ctx.empty(S * T, 32)
+        off = [s * T for s in range(S + 1)]
+        C.io_chain(ctx, leaves, tok, ph, off, out=io_out)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        C.io_chain(ctx, leaves, tok, ph, off, out=io_out)
+        b.record(stream)
+        torch.cuda.synchronize()
+        io_ms = a.elapsed_time(b)
+        io_chain = {"chains": S, "tokens_per_chain": T, "ms": round(io_ms, 3),
+                    "ns_per_token": round(io_ms * 1e6 / T, 1)}
+        if rank == 0 and world == 1 and not args.no_cpu:
+            import numpy as np
+            from oracle import vco
+            lh, th = leaves[:T].cpu().numpy(), tok[:T].cpu().numpy().view(np.uint32)
+            t_c = time.perf_counter()
+            vco.io_chain(lh, th, b"synthetic prompt 0")
+            io_chain["cpu_ms_one_chain"] = round((time.perf_counter() - t_c) * 1e3, 3)
+        del leaves, tok, io_out
+
     # integer-ALU peak probe on the same GPU, same run
     peak_ops = C.int_peak(ctx, 0, 4000)
     ctx.sync(timeout_ms=600000)
@@ -602,6 +632,7 @@ def main():
                              "frac": round(hbm_achieved / hbm, 4), "peak_source": "MEASURED_PEAKS.json hbm_gbs"}},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "io_chain": io_chain,
         "gpu_launches": args.steps * step.launches,
         "clocks": clk.summary(),
     }

@@ -87,8 +87,7 @@ struct TraceArgs {
 };
 cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s);
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
-                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io,
-                            cudaStream_t s);
+                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, cudaStream_t s);
 cudaError_t launch_tagged_hash(int n, int tag, const uint8_t* data, const int64_t* off_dev,
                                int64_t fixed_len, uint8_t* out, cudaStream_t s);
 

@@ -201,13 +201,17 @@ class KvStep:
     def host_inputs(self):
         return list(self.view.k_layers) + list(self.view.v_layers)
 
-    def e2e_step(self, dev_tensors, roots_host):
+    def e2e_step(self, host, dev_tensors, roots_host):
+        """Public host-buffer API: layer groups copied while earlier groups hash."""
         C = self.C
         L = self.w["n_layers"]
-        view = C.KvCacheView(dev_tensors[:L], dev_tensors[L:], self.view.seq_lens,
-                             block_tables=self.view.block_tables)
-        roots, trees = C.kv_commit(self.ctx, view, keep_trees=True, roots_out=self.roots)
-        roots_host.copy_(roots.view(-1), non_blocking=True)
+        if not hasattr(self, "_copy_stream"):
+            self._copy_stream = self.torch.cuda.Stream(self.ctx.device)
+        roots, trees = C.kv_commit_host(self.ctx, host[:L], host[L:], self.view.seq_lens,
+                                        block_tables=self.view.block_tables, dev_k=dev_tensors[:L],
+                                        dev_v=dev_tensors[L:], roots_out=self.roots, copy_stream=self._copy_stream)
+        with self.torch.cuda.stream(self.stream):
+            roots_host.copy_(roots.view(-1), non_blocking=True)
         trees.free()
         return roots.numel()
 
@@ -296,7 +300,10 @@ class TraceStep:
             out.insert(1, self.x)
         return out
 
-    def e2e_step(self, dev_tensors, roots_host):
+    def e2e_step(self, host, dev_tensors, roots_host):
+        with self.torch.cuda.stream(self.stream):
+            for d, h in zip(dev_tensors, host):
+                d.copy_(h, non_blocking=True)
         if self.x is not None:
             a, x, sa, sx, logits, tok, seeds = dev_tensors
         else:
@@ -570,9 +577,7 @@ def main():
 
         def e2e_step():
             with torch.cuda.stream(stream):
-                for d, h in zip(dev, host):
-                    d.copy_(h, non_blocking=True)
-                return estep.e2e_step(dev, roots_host)
+                return estep.e2e_step(host, dev, roots_host)
 
         for _ in range(3 if w["kind"] == "kv" else 1):
             e2e_step()

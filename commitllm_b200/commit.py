@@ -278,6 +278,81 @@ def kv_commit(ctx: Context, view: KvCacheView, keep_trees: bool = True,
     return roots_out, (TreeSet(ctx, h) if keep_trees else None)
 
 
+class TreeGroups:
+    """Tree sets of a KV commit done in layer groups; tree (s, l) lookups dispatch to the group."""
+
+    def __init__(self, groups, n_seqs):
+        self.groups = groups          # [(layer_begin, layer_end, TreeSet)]
+        self.n_seqs = n_seqs
+
+    def locate(self, seq: int, layer: int):
+        for lb, le, ts in self.groups:
+            if lb <= layer < le:
+                return ts, seq * (le - lb) + (layer - lb)
+        raise IndexError(f"layer {layer} not committed")
+
+    def prove(self, seq: int, layer: int, positions: Sequence[int]):
+        ts, t = self.locate(seq, layer)
+        return ts.prove([t] * len(positions), positions)
+
+    def free(self) -> None:
+        for _, _, ts in self.groups:
+            ts.free()
+
+
+def kv_commit_host(ctx: Context, k_host: Sequence[torch.Tensor], v_host: Sequence[torch.Tensor],
+                   seq_lens: Sequence[int], block_tables: Optional[torch.Tensor] = None,
+                   seq_row_offset: Optional[Sequence[int]] = None, layer_base: int = 0, n_groups: int = 4,
+                   dev_k: Optional[Sequence[torch.Tensor]] = None, dev_v: Optional[Sequence[torch.Tensor]] = None,
+                   roots_out: Optional[torch.Tensor] = None, keep_trees: bool = True,
+                   copy_stream: Optional[torch.cuda.Stream] = None):
+    """kv_commit of a K/V transcript held in host memory (pinned for overlap).
+
+    Layers are copied to the device in ``n_groups`` groups on a copy stream;
+    each group is hashed on the context's stream as soon as its copy lands,
+    while the next group is in flight.  ``dev_k``/``dev_v`` (same shapes on
+    the device) are reused when given.  Returns ``(roots [n_seqs, n_layers,
+    32], TreeGroups or None)``.
+    """
+    L = len(k_host)
+    if L == 0 or L != len(v_host):
+        raise ValueError("k_host and v_host must be non-empty and of equal length")
+    dev = f"cuda:{ctx.device}"
+    if dev_k is None:
+        dev_k = [torch.empty_like(t, device=dev) for t in k_host]
+    if dev_v is None:
+        dev_v = [torch.empty_like(t, device=dev) for t in v_host]
+    S = len(seq_lens)
+    if roots_out is None:
+        roots_out = ctx.empty(S, L, 32)
+    cs = copy_stream if copy_stream is not None else torch.cuda.Stream(ctx.device)
+    n_groups = max(1, min(n_groups, L))
+    bounds = [L * i // n_groups for i in range(n_groups + 1)]
+    groups = []
+    cs.wait_stream(ctx.stream)     # the device buffers may still be read by earlier work
+    for g in range(n_groups):
+        lb, le = bounds[g], bounds[g + 1]
+        with torch.cuda.stream(cs):
+            for l in range(lb, le):
+                dev_k[l].copy_(k_host[l], non_blocking=True)
+                dev_v[l].copy_(v_host[l], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+        ctx.stream.wait_event(ev)
+        view = KvCacheView(dev_k[lb:le], dev_v[lb:le], seq_lens, block_tables=block_tables,
+                           seq_row_offset=seq_row_offset, layer_base=layer_base + lb)
+        if S == 1:
+            out = roots_out[:, lb:le]
+            r, ts = kv_commit(ctx, view, keep_trees=keep_trees, roots_out=out)
+        else:
+            r, ts = kv_commit(ctx, view, keep_trees=keep_trees, roots_out=ctx.empty(S, le - lb, 32))
+            with torch.cuda.stream(ctx.stream):
+                roots_out[:, lb:le].copy_(r.view(S, le - lb, 32))
+        if keep_trees:
+            groups.append((lb, le, ts))
+    return roots_out, (TreeGroups(groups, S) if keep_trees else None)
+
+
 # ---------------------------------------------------------------------------
 # Trees, IO chain, trace leaves
 # ---------------------------------------------------------------------------

@@ -220,3 +220,22 @@ def test_invalid_arguments(ctx):
     view.seq_lens = [5]   # more rows than the buffer holds
     with pytest.raises(VcValueError):
         C.kv_commit(ctx, view)
+
+
+@pytest.mark.parametrize("paged_case", [False, True])
+def test_host_buffer_commit_matches_device_commit(ctx, paged_case):
+    """kv_commit_host pipelines layer groups from host memory; roots and proofs equal kv_commit's."""
+    import torch
+    tr = kvref.paged(71, 5, [40, 300], 2, 64) if paged_case else kvref.contiguous(72, 5, [333], 4, 32)
+    view = tr.view(ctx.device)
+    want, wtrees = C.kv_commit(ctx, view, keep_trees=True)
+    host_k = [t.cpu().pin_memory() for t in view.k_layers]
+    host_v = [t.cpu().pin_memory() for t in view.v_layers]
+    got, groups = C.kv_commit_host(ctx, host_k, host_v, tr.seq_lens, block_tables=view.block_tables, n_groups=3)
+    ctx.sync(timeout_ms=60000)
+    assert torch.equal(got, want)
+    s, l = len(tr.seq_lens) - 1, 4
+    sib, depth = groups.prove(s, l, [0, 7, tr.seq_lens[s] - 1])
+    sib2, depth2 = wtrees.prove([s * 5 + l] * 3, [0, 7, tr.seq_lens[s] - 1])
+    assert depth == depth2 and torch.equal(sib, sib2)
+    groups.free()

@@ -35,6 +35,9 @@ sys.path.insert(0, ROOT)
 
 BLK_OPS = 1384          # int32 ops per SHA-256 block (one compression), see DESIGN.md
 METRIC = "trace bytes committed GB/s"
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel, from the ncu capture summarised in profiles/ (bytes, source)
+TRAFFIC = {"c2": (560.3e6, "profiles/kv_commit_llama8b.md (ncu, same workload)")}
 WORKLOADS = {
     "c2": dict(kind="kv", name="llama3.1-8b-kv", n_layers=32, n_heads=8, head_dim=128, n_seqs=1, seq_len=4096,
                paged=False, steps=400),
@@ -629,7 +632,10 @@ def main():
         "roots_per_s": round(n_roots * world / (ms_step * 1e-3), 2),
         "hashed_msg_GBps": round(msg_bytes * world / (ms_step * 1e-3) / 1e9, 3),
         "roofline": {"bound": "int_alu", "achieved": round(alu_achieved, 3), "peak": round(alu_peak, 3),
-                     "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4), "traffic": None,
+                     "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4),
+                     "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not args.seqs else None,
+                     "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC and not args.seqs else None,
+                     "algorithmic_bytes": src_bytes,
                      "kernel": "kv_commit_kernel" if w["kind"] == "kv" else "trace_leaf_kernel",
                      "kernel_ms": round(k_avg, 4), "sha_blocks": blocks, "ops_per_block": BLK_OPS,
                      "peak_source": "vc_int_peak SHA-mix probe, this GPU, this run",

@@ -278,6 +278,32 @@ def kv_commit(ctx: Context, view: KvCacheView, keep_trees: bool = True,
     return roots_out, (TreeSet(ctx, h) if keep_trees else None)
 
 
+def kv_open(ctx: Context, view: KvCacheView, trees: TreeSet, seq: int, layers: Sequence[int],
+            n_positions: int):
+    """KV openings of open_v4 (prover/src/lib.rs:1564-1588) for one sequence.
+
+    For each layer in ``layers`` and every position 0..n_positions-1: the
+    ``KvEntry`` (K and V rows widened to f64) and its Merkle proof against
+    that layer's kv_root.  Returns ``(entries f64 [n_sel, n_pos, 2, kv_dim],
+    siblings uint8 [n_sel, n_pos, depth, 32], depth)``, all on the device.
+    ``view`` and ``trees`` must be the ones the commit used, with the cache
+    rows unchanged since.
+    """
+    d, keep = _kv_desc(view)
+    kv = d.n_kv_heads * d.head_dim
+    n_sel = len(layers)
+    n = int(view.seq_lens[seq]) if 0 <= seq < len(view.seq_lens) else 1
+    depth_max = max(1, (1 << (n - 1).bit_length()).bit_length() - 1) if n > 1 else 1
+    entries = ctx.empty(max(n_sel, 1), max(n_positions, 1), 2, kv, dtype=torch.float64)
+    sib = ctx.empty(max(n_sel, 1), max(n_positions, 1), depth_max, 32)
+    depth = ctypes.c_int32(0)
+    check(lib().vc_kv_open(ctx.handle, ctypes.byref(d), trees._h, int(seq), n_sel, _i32(layers), int(n_positions),
+                           ctypes.c_void_p(entries.data_ptr()), ctypes.c_void_p(sib.data_ptr()), depth_max,
+                           ctypes.byref(depth)))
+    del keep
+    return entries[:n_sel, :n_positions], sib[:n_sel, :n_positions, : depth.value], depth.value
+
+
 class TreeGroups:
     """Tree sets of a KV commit done in layer groups; tree (s, l) lookups dispatch to the group."""
 

@@ -482,6 +482,80 @@ vc_status vc_prove(vc_ctx* c, const vc_tree_set* ts, int32_t n, const int32_t* t
   return VC_OK;
 }
 
+vc_status vc_kv_open(vc_ctx* c, const vc_kv_desc* d, const vc_tree_set* ts, int32_t seq, int32_t n_sel,
+                     const int32_t* layers, int32_t n_positions, double* entries_dev, uint8_t* siblings_dev,
+                     int32_t max_depth, int32_t* depth_out) {
+  if (!c || !d || !ts || !layers || (n_sel > 0 && n_positions > 0 && (!entries_dev || !siblings_dev)))
+    return fail(VC_EINVAL, "vc_kv_open: NULL argument");
+  if (n_sel < 0 || n_positions < 0) return fail(VC_EINVAL, "vc_kv_open: negative count");
+  if (seq < 0 || seq >= d->n_seqs) return fail(VC_ERANGE, "vc_kv_open: seq %d of %d", seq, d->n_seqs);
+  if (int64_t(d->n_seqs) * d->n_layers != int64_t(ts->node_base.size()))
+    return fail(VC_EINVAL, "vc_kv_open: tree set does not match the descriptor (%zu trees, %d x %d)",
+                ts->node_base.size(), d->n_seqs, d->n_layers);
+  if (n_positions > d->seq_lens[seq])
+    return fail(VC_ERANGE, "vc_kv_open: %d positions of a %d-token sequence", n_positions, d->seq_lens[seq]);
+  if (!d->k_layers || !d->v_layers || d->cache_elems <= 0) return fail(VC_EINVAL, "vc_kv_open: bad descriptor");
+  for (int i = 0; i < n_sel; ++i)
+    if (layers[i] < 0 || layers[i] >= d->n_layers) return fail(VC_ERANGE, "vc_kv_open: layer %d of %d", layers[i], d->n_layers);
+  if (n_sel == 0 || n_positions == 0) return VC_OK;
+  const int64_t n = int64_t(n_sel) * n_positions;
+  if (n > 0x7FFFFFFF) return fail(VC_EINVAL, "vc_kv_open: too many openings");
+  // proofs: the batched merkle::prove of every (layer, position)
+  std::vector<int32_t> tree(n);
+  std::vector<uint32_t> leaf(n);
+  for (int i = 0; i < n_sel; ++i)
+    for (int p = 0; p < n_positions; ++p) {
+      tree[int64_t(i) * n_positions + p] = seq * d->n_layers + layers[i];
+      leaf[int64_t(i) * n_positions + p] = uint32_t(p);
+    }
+  std::vector<int32_t> depth(n);
+  vc_status r = vc_prove(c, ts, int32_t(n), tree.data(), leaf.data(), siblings_dev, max_depth, depth.data());
+  if (r) return r;
+  if (depth_out) *depth_out = depth[0];
+  // entries: the rows widened to f64
+  int64_t r0 = 0;
+  if (!d->block_tables) {
+    if (d->seq_row_offset) {
+      r0 = d->seq_row_offset[seq];
+    } else {
+      for (int s = 0; s < seq; ++s) r0 += d->seq_lens[s];
+    }
+  }
+  DeviceGuard g(c->device);
+  Stager st;
+  const size_t o_k = st.add(d->k_layers, sizeof(void*) * d->n_layers);
+  const size_t o_v = st.add(d->v_layers, sizeof(void*) * d->n_layers);
+  const size_t o_l = st.add(layers, sizeof(int32_t) * n_sel);
+  char* dev = nullptr;
+  r = upload(c, st, &dev);
+  if (r) return r;
+  KvOpenArgs a{};
+  a.kv.k_layers = reinterpret_cast<const void* const*>(dev + o_k);
+  a.kv.v_layers = reinterpret_cast<const void* const*>(dev + o_v);
+  a.kv.block_tables = d->block_tables;
+  a.kv.stride_page = d->stride_page;
+  a.kv.stride_row = d->stride_row;
+  a.kv.stride_head = d->stride_head;
+  a.kv.block_size = d->block_tables ? d->block_size : 1;
+  a.kv.max_blocks = d->max_blocks_per_seq;
+  a.kv.n_heads = d->n_kv_heads;
+  a.kv.head_dim = d->head_dim;
+  a.kv.paged = d->block_tables ? 1 : 0;
+  a.kv.cache_elems = d->cache_elems;
+  a.kv.row_span = int64_t(d->n_kv_heads - 1) * d->stride_head + d->head_dim;
+  a.kv.err = c->err;
+  a.seq.seq = seq;
+  a.seq.src_off = r0;
+  a.layers = reinterpret_cast<const int32_t*>(dev + o_l);
+  a.n_sel = n_sel;
+  a.n_pos = n_positions;
+  a.kv_dim = d->n_kv_heads * d->head_dim;
+  a.out = entries_dev;
+  const cudaError_t e = launch_kv_entries(a, d->dtype, c->stream);
+  if (e != cudaSuccess) return fail(VC_ECUDA, "vc_kv_open launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
 int32_t vc_tree_set_count(const vc_tree_set* ts) { return ts ? int32_t(ts->node_base.size()) : 0; }
 
 vc_status vc_tree_nodes(const vc_tree_set* ts, int32_t tree, const uint8_t** nodes_dev, int64_t* n_leaves,

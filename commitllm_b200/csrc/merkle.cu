@@ -759,6 +759,49 @@ extern "C" vc_status vc_kv_commit_noalloc(const vc_kv_desc* d, uint8_t* kv_roots
 
 namespace vc {
 
+// KvEntry {k_roped, v_deq} of every (selected layer, position): the rows the
+// leaves hashed, widened to f64 exactly as the leaf kernel widens them.  One
+// CTA per (layer, position), threads stride over the kv_dim elements.
+template <int DT>
+__global__ void kv_entries_kernel(KvOpenArgs a) {
+  const int sel = blockIdx.x / a.n_pos;
+  const int pos = blockIdx.x % a.n_pos;
+  const int layer = a.layers[sel];
+  const int64_t row = kv_row(a.kv, a.seq, pos);
+  double* out = a.out + (int64_t(sel) * a.n_pos + pos) * 2 * a.kv_dim;
+  for (int e = threadIdx.x; e < 2 * a.kv_dim; e += blockDim.x) {
+    double v = 0.0;
+    if (row >= 0) {
+      const int sel_v = e >= a.kv_dim;
+      const int i = sel_v ? e - a.kv_dim : e;
+      const int h = i / a.kv.head_dim, dd = i % a.kv.head_dim;
+      const int64_t off = row + int64_t(h) * a.kv.stride_head + dd;
+      const void* base = sel_v ? a.kv.v_layers[layer] : a.kv.k_layers[layer];
+      if (DT == 0) {
+        v = double(__uint_as_float(uint32_t(__ldg(static_cast<const uint16_t*>(base) + off)) << 16));
+      } else if (DT == 1) {
+        uint32_t hi, lo;
+        f32_to_f64_bits(__ldg(static_cast<const uint32_t*>(base) + off), hi, lo);
+        v = __hiloint2double(int(hi), int(lo));
+      } else {
+        v = __ldg(static_cast<const double*>(base) + off);
+      }
+    }
+    out[e] = v;
+  }
+}
+
+cudaError_t launch_kv_entries(const KvOpenArgs& a, int dtype, cudaStream_t s) {
+  const int64_t n = int64_t(a.n_sel) * a.n_pos;
+  if (n == 0) return cudaSuccess;
+  switch (dtype) {
+    case 0: kv_entries_kernel<0><<<int(n), 128, 0, s>>>(a); break;
+    case 1: kv_entries_kernel<1><<<int(n), 128, 0, s>>>(a); break;
+    default: kv_entries_kernel<2><<<int(n), 128, 0, s>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_zero_roots(uint32_t* z, cudaStream_t s) {
   zero_roots_kernel<<<1, 32, 0, s>>>(z);
   return cudaGetLastError();

@@ -63,7 +63,17 @@ struct ProveReq {
   int32_t log2_pad;
 };
 
+// KvEntry materialisation for openings: (layer sel, position) -> f64 K row, f64 V row.
+struct KvOpenArgs {
+  KvArgs kv;               // addressing of the committed transcript (k_layers/v_layers device tables)
+  TreeMeta seq;            // the opened sequence (seq index, src_off)
+  const int32_t* layers;   // [n_sel] layer indices (within the call's layers)
+  int32_t n_sel, n_pos, kv_dim;
+  double* out;             // [n_sel][n_pos][2][kv_dim]
+};
+
 cudaError_t launch_zero_roots(uint32_t* z, cudaStream_t s);
+cudaError_t launch_kv_entries(const KvOpenArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_kv_commit(const KvArgs& a, int n_items, int n_layers, int dtype, bool fast,
                              cudaStream_t s);
 cudaError_t launch_tree_commit(const TreeArgs& a, int n_items, cudaStream_t s);

@@ -22,6 +22,7 @@ Openings of the committed trees are available as ``*_proof`` methods.
 from __future__ import annotations
 
 import json
+import struct
 from typing import List, Optional, Sequence
 
 import numpy as np
@@ -77,6 +78,7 @@ class _Committed:
         self._kv_roots = kv_roots        # device [n_layers, 32] or None
         self._kv_trees = kv_trees
         self._n_kv_layers = n_kv_layers
+        self._kv_view = None
         self._host = None
 
     def _h(self):
@@ -144,6 +146,52 @@ class _Committed:
             raise ValueError(f"layer {layer} out of range")
         return self._proof(self._kv_trees, layer, position)
 
+    # --- KV openings of open_v4 (prover/src/lib.rs:1564-1588) ---
+    def kv_openings(self, token_index: int, layer_indices: Optional[Sequence[int]] = None):
+        """``(entries f64 [n_sel, t+1, 2, kv_dim], siblings uint8 [n_sel, t+1, depth, 32])`` on the host.
+
+        Entry [i][p] is the ``KvEntry`` of layer ``layer_indices[i]`` at position
+        p (``k_roped`` = [..., 0, :], ``v_deq`` = [..., 1, :]); the proof
+        verifies ``hash_kv_entry(layer, p, k, v)`` against ``kv_roots[layer]``.
+        """
+        if self._kv_trees is None:
+            raise ValueError("no KV transcript was committed")
+        if not 0 <= token_index < self._kv_view.seq_lens[0]:
+            raise ValueError(f"token_index {token_index} out of range")
+        layers = list(range(self._n_kv_layers)) if layer_indices is None else [int(l) for l in layer_indices]
+        layers = [l for l in layers if 0 <= l < self._n_kv_layers]   # open_v4 skips unknown layers
+        ent, sib, _ = C.kv_open(self._ctx, self._kv_view, self._kv_trees, 0, layers, token_index + 1)
+        self._ctx.sync()
+        return layers, ent.cpu().numpy(), sib.cpu().numpy()
+
+    def audit_kv_json(self, token_index: int, layer_indices: Optional[Sequence[int]] = None) -> str:
+        """The ``kv_entries`` / ``kv_proofs`` fields of ``V4AuditResponse`` in serde_json form
+        (f64 as little-endian hex, ``f64_hex_vec`` in types.rs:1253-1317)."""
+        _layers, ent, sib = self.kv_openings(token_index, layer_indices)
+        entries = [[{"k_roped": [x.tobytes().hex() for x in e[0].astype("<f8")],
+                     "v_deq": [x.tobytes().hex() for x in e[1].astype("<f8")]} for e in layer] for layer in ent]
+        proofs = [[{"leaf_index": p, "siblings": [list(map(int, s)) for s in layer[p]]}
+                   for p in range(layer.shape[0])] for layer in sib]
+        return json.dumps({"kv_entries": entries, "kv_proofs": proofs}, separators=(",", ":"))
+
+    def audit_kv_bincode(self, token_index: int, layer_indices: Optional[Sequence[int]] = None) -> bytes:
+        """bincode v1 of ``Some(kv_entries)`` then ``Some(kv_proofs)``, the bytes these two
+        ``V4AuditResponse`` fields take inside a VV4A receipt (serialize.rs:43-50)."""
+        _layers, ent, sib = self.kv_openings(token_index, layer_indices)
+        out = bytearray(b"\x01") + struct.pack("<Q", ent.shape[0])
+        kv = ent.shape[-1]
+        for layer in ent:
+            out += struct.pack("<Q", layer.shape[0])
+            for e in layer:
+                out += struct.pack("<Q", kv) + e[0].astype("<f8").tobytes()
+                out += struct.pack("<Q", kv) + e[1].astype("<f8").tobytes()
+        out += b"\x01" + struct.pack("<Q", sib.shape[0])
+        for layer in sib:
+            out += struct.pack("<Q", layer.shape[0])
+            for p in range(layer.shape[0]):
+                out += struct.pack("<IQ", p, layer.shape[1]) + layer[p].tobytes()
+        return bytes(out)
+
     def leaf_hashes(self) -> torch.Tensor:
         """The retained leaves (tree 0's level 0), a device view ``[n_tokens, 32]``."""
         return self._trees.nodes(0)[: self._n_tokens]
@@ -207,7 +255,9 @@ def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens
         r, kv_trees = C.kv_commit(ctx, kv_cache, keep_trees=True)
         kv_roots = r[0]
         n_kv_layers = len(kv_cache.k_layers)
-    return handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers, **extra)
+    h = handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers, **extra)
+    h._kv_view = kv_cache
+    return h
 
 
 def _wrap_rows(n_tokens, rows, n_prompt_tokens, which):

@@ -256,6 +256,23 @@ VC_API vc_status vc_prove(vc_ctx* ctx, const vc_tree_set* trees, int32_t n, cons
                    const uint32_t* leaf, uint8_t* siblings_dev, int32_t max_depth,
                    int32_t* depth_out);
 
+/*
+ * KV openings of one sequence, as open_v4 returns them
+ * (crates/verilm-prover/src/lib.rs:1564-1588): for each selected layer
+ * (layers[i], HOST, indices into desc's layers) and every position
+ * p in 0..n_positions-1 (the challenged token index + 1):
+ *   entries_dev[i][p] = KvEntry { k_roped: f64[kv_dim], v_deq: f64[kv_dim] }
+ *     (types.rs:1244-1251), the rows the leaf hashed, widened as hashed;
+ *     DEVICE f64 [n_sel][n_positions][2][kv_dim];
+ *   siblings_dev[i][p] = merkle::prove(kv_tree[layer], p).siblings
+ *     (merkle.rs:79-99), DEVICE [n_sel][n_positions][max_depth][32].
+ * trees: the tree set vc_kv_commit returned for the same descriptor.
+ * *depth_out: the proof length (log2 of the sequence's padded length).
+ */
+VC_API vc_status vc_kv_open(vc_ctx* ctx, const vc_kv_desc* desc, const vc_tree_set* trees, int32_t seq,
+                            int32_t n_sel, const int32_t* layers, int32_t n_positions, double* entries_dev,
+                            uint8_t* siblings_dev, int32_t max_depth, int32_t* depth_out);
+
 /* Shape of a tree set: number of trees. */
 VC_API int32_t vc_tree_set_count(const vc_tree_set* trees);
 /*

@@ -239,3 +239,49 @@ def test_host_buffer_commit_matches_device_commit(ctx, paged_case):
     sib2, depth2 = wtrees.prove([s * 5 + l] * 3, [0, 7, tr.seq_lens[s] - 1])
     assert depth == depth2 and torch.equal(sib, sib2)
     groups.free()
+
+
+def test_kv_openings_verify_like_the_verifier(ctx):
+    """open_v4's KV part: every returned KvEntry re-hashes (hash_kv_entry) to a leaf whose
+    proof verifies against kv_roots[layer] -- verify_kv_entry_provenance's check."""
+    tr = kvref.paged(81, 4, [150], 2, 32, block_size=16)
+    view = tr.view(ctx.device)
+    roots, trees = C.kv_commit(ctx, view, keep_trees=True)
+    layers, t = [3, 0], 149
+    ent, sib, depth = C.kv_open(ctx, view, trees, 0, layers, t + 1)
+    ctx.sync(timeout_ms=60000)
+    ent, sib, roots = ent.cpu().numpy(), sib.cpu().numpy(), roots.cpu().numpy()
+    assert depth == 8 and ent.shape == (2, 150, 2, 64)
+    for i, l in enumerate(layers):
+        for p in range(0, t + 1, 7):
+            leaf = O.hash_kv_entry(l, p, ent[i, p, 0], ent[i, p, 1])
+            assert O.verify(bytes(roots[0, l]), leaf, O.MerkleProof(p, [bytes(x) for x in sib[i, p]]))
+        # entries are the cache rows widened exactly
+        pg = tr.block_tables[0, 5 // 16]
+        want = O.bf16_to_f64(tr.k[l, pg, 5 % 16].reshape(-1))
+        assert np.array_equal(ent[i, 5, 0].view(np.uint64), want.view(np.uint64))
+
+
+def test_audit_kv_encodings(ctx):
+    """kv_entries / kv_proofs in serde_json (f64 hex) and bincode form, via the drop-in handle."""
+    import struct
+    from commitllm_b200 import verilm_rs as V
+    tr = kvref.contiguous(82, 2, [9], 1, 8)
+    view = tr.view(ctx.device)
+    a = np.zeros((9, 2, 4), np.int8)
+    h = V.commit_minimal_from_captures([a[t, l] for t in range(9) for l in range(2)],
+                                       np.ones(9 * 2 * 4, np.float32), 2, [1] * 9, list(range(9)), b"p", b"\0" * 32,
+                                       kv_cache=view, ctx=ctx)
+    js = json.loads(h.audit_kv_json(4, [1]))
+    assert len(js["kv_entries"]) == 1 and len(js["kv_entries"][0]) == 5
+    e = js["kv_entries"][0][4]
+    k = np.frombuffer(bytes.fromhex("".join(e["k_roped"])), dtype="<f8")
+    v = np.frombuffer(bytes.fromhex("".join(e["v_deq"])), dtype="<f8")
+    leaf = O.hash_kv_entry(1, 4, k, v)
+    pr = js["kv_proofs"][0][4]
+    assert O.verify(bytes.fromhex(h.kv_roots_hex()[1]), leaf, O.MerkleProof(pr["leaf_index"], [bytes(s) for s in pr["siblings"]]))
+    b = h.audit_kv_bincode(4, [1])
+    # Some(vec of 1 layer) of 5 entries, first entry's k_roped length 8
+    assert b[0] == 1 and struct.unpack_from("<QQQ", b, 1) == (1, 5, 8)
+    k0 = bytes.fromhex("".join(js["kv_entries"][0][0]["k_roped"]))
+    assert b[25:25 + 64] == k0                                   # entry 0's k_roped, raw f64 LE

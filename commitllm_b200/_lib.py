@@ -15,12 +15,14 @@ LIB_PATH = os.path.join(HERE, "libvcommit.so")
 
 VC_OK, VC_EINVAL, VC_ENOMEM, VC_ECUDA, VC_ETIMEDOUT, VC_ERANGE, VC_ENOTSUP = range(7)
 VC_DTYPE_BF16, VC_DTYPE_F32, VC_DTYPE_F64 = 0, 1, 2
+VC_ROPE_NONE, VC_ROPE_LLAMA3, VC_ROPE_LINEAR = 0, 1, 2
 
 SYMBOLS = (
     "vc_abi_version", "vc_last_error", "vc_ctx_create", "vc_ctx_destroy", "vc_ctx_sync",
     "vc_kv_commit", "vc_trace_leaves", "vc_io_chain", "vc_prompt_hash", "vc_seed_commitment",
     "vc_build_trees", "vc_prove", "vc_tree_set_count", "vc_tree_nodes", "vc_tree_set_free",
-    "vc_int_peak", "vc_kv_commit_noalloc", "vc_kv_open",
+    "vc_int_peak", "vc_kv_commit_noalloc", "vc_kv_open", "vc_io_extend", "vc_io_genesis",
+    "vc_kv_transcript",
 )
 
 
@@ -63,6 +65,21 @@ class TraceDesc(ctypes.Structure):
     ]
 
 
+class KvtDesc(ctypes.Structure):
+    _fields_ = [
+        ("n_tokens", c_int32), ("n_layers", c_int32), ("hidden", c_int32), ("n_kv_heads", c_int32),
+        ("head_dim", c_int32), ("use_rope", c_int32),
+        ("x_layers", POINTER(c_void_p)), ("x_row_stride", c_int64),
+        ("wk_layers", POINTER(c_void_p)), ("wv_layers", POINTER(c_void_p)),
+        ("scale_x", c_void_p), ("sx_tstride", c_int64), ("sx_lstride", c_int64),
+        ("sw_k", POINTER(ctypes.c_float)), ("sw_v", POINTER(ctypes.c_float)),
+        ("ch_k", POINTER(c_void_p)), ("ch_v", POINTER(c_void_p)),
+        ("bias_k", POINTER(c_void_p)), ("bias_v", POINTER(c_void_p)),
+        ("rope_theta", c_double), ("rope_scaling", c_int32), ("rope_original_max_position_embeddings", c_int32),
+        ("rope_factor", c_double), ("rope_low_freq_factor", c_double), ("rope_high_freq_factor", c_double),
+    ]
+
+
 _lib = None
 _load_error = None
 
@@ -80,6 +97,8 @@ def _declare(lib):
         "vc_kv_commit": [P, POINTER(KvDesc), P, POINTER(P)],
         "vc_trace_leaves": [P, POINTER(TraceDesc), P],
         "vc_io_chain": [P, c_int32, POINTER(c_int64), P, P, P, P],
+        "vc_io_extend": [P, c_int32, POINTER(c_int64), P, P, P, P],
+        "vc_io_genesis": [P, c_int32, P, P],
         "vc_prompt_hash": [P, c_int32, P, POINTER(c_int64), P],
         "vc_seed_commitment": [P, c_int32, P, P],
         "vc_build_trees": [P, c_int32, POINTER(c_int64), P, P, POINTER(P)],
@@ -90,6 +109,7 @@ def _declare(lib):
         "vc_kv_commit_noalloc": [POINTER(KvDesc), P, P, P],
         "vc_kv_open": [P, POINTER(KvDesc), P, c_int32, c_int32, POINTER(c_int32), c_int32, P, P, c_int32,
                        POINTER(c_int32)],
+        "vc_kv_transcript": [P, POINTER(KvtDesc), P, P],
     }.items():
         fn = getattr(lib, name)
         fn.restype = c_int32

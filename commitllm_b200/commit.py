@@ -530,3 +530,136 @@ def int_peak(ctx: Context, variant: int = 0, iters: int = 20000) -> float:
     v = ctypes.c_double()
     check(lib().vc_int_peak(ctx.handle, int(variant), int(iters), ctypes.byref(v)))
     return v.value
+
+
+# --------------------------------------------------------------------------
+# KV transcript: compute_kv_transcript (crates/verilm-prover/src/lib.rs:207-329)
+# --------------------------------------------------------------------------
+
+@dataclass
+class RopeConfig:
+    """RoPE part of ``ModelConfig`` (crates/verilm-core/src/constants.rs:126-156):
+    ``theta`` and the optional scaling (``"llama3"``, ``"linear"``; any other
+    type leaves the frequencies unscaled, constants.rs:292-295)."""
+    theta: float = 10000.0
+    scaling: Optional[str] = None
+    factor: float = 8.0
+    low_freq_factor: float = 1.0
+    high_freq_factor: float = 4.0
+    original_max_position_embeddings: int = 8192
+
+
+@dataclass
+class KvTranscriptInputs:
+    """Device-resident inputs of one transcript.
+
+    x_attn: per layer an int8 ``[n_tokens, hidden]`` view (row stride a
+    multiple of 16 bytes, the same for every layer) or one
+    ``[n_layers, n_tokens, hidden]`` tensor; wk, wv: per layer int8
+    ``[kv_dim, hidden]`` row-major; scale_x: float32 ``[n_tokens, n_layers]``
+    (any strides).  per_tensor: per layer ``(sw_k, sw_v)``; per_channel: per
+    layer ``(cw_k, cw_v)`` float32 device tensors or None; biases: per layer
+    ``(b_k, b_v)`` float32 device tensors or None.  With neither scale list
+    the reference's toy path applies (clamp to int8).
+    """
+    x_attn: object
+    wk: Sequence[torch.Tensor]
+    wv: Sequence[torch.Tensor]
+    scale_x: Optional[torch.Tensor]
+    n_kv_heads: int
+    head_dim: int
+    per_tensor: Optional[Sequence] = None
+    per_channel: Optional[Sequence] = None
+    biases: Optional[Sequence] = None
+    rope: Optional[RopeConfig] = None
+
+
+def kv_transcript(ctx: Context, inp: KvTranscriptInputs, k_out: Optional[torch.Tensor] = None,
+                  v_out: Optional[torch.Tensor] = None):
+    """``k_roped, v_deq``: float64 ``[n_layers, n_tokens, kv_dim]`` device tensors."""
+    xs = list(inp.x_attn) if not isinstance(inp.x_attn, torch.Tensor) else [x for x in inp.x_attn]
+    n_layers = len(xs)
+    if n_layers < 1 or len(inp.wk) != n_layers or len(inp.wv) != n_layers:
+        raise ValueError("x_attn, wk and wv must have one entry per layer")
+    n_tok, hidden = int(xs[0].shape[0]), int(xs[0].shape[1])
+    stride = int(xs[0].stride(0))
+    for x in xs:
+        _require_cuda(x, "x_attn")
+        if x.dtype != torch.int8 or tuple(x.shape) != (n_tok, hidden) or x.stride(1) != 1 or x.stride(0) != stride:
+            raise ValueError("x_attn layers must be int8 [n_tokens, hidden] views with one common row stride")
+    kv = int(inp.n_kv_heads) * int(inp.head_dim)
+    for w in list(inp.wk) + list(inp.wv):
+        _require_cuda(w, "weight")
+        if w.dtype != torch.int8 or tuple(w.shape) != (kv, hidden) or not w.is_contiguous():
+            raise ValueError(f"Wk/Wv must be contiguous int8 [{kv}, {hidden}]")
+    use_rope = bool(inp.per_tensor) or bool(inp.per_channel)
+    keep = []
+
+    def pp(arr):
+        keep.append(arr)
+        return ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
+
+    d = _lib.KvtDesc()
+    d.n_tokens, d.n_layers, d.hidden = n_tok, n_layers, hidden
+    d.n_kv_heads, d.head_dim, d.use_rope = int(inp.n_kv_heads), int(inp.head_dim), int(use_rope)
+    d.x_layers = pp(_ptrs([x.data_ptr() for x in xs]))
+    d.x_row_stride = stride
+    d.wk_layers = pp(_ptrs([w.data_ptr() for w in inp.wk]))
+    d.wv_layers = pp(_ptrs([w.data_ptr() for w in inp.wv]))
+    if use_rope and n_tok > 0:
+        sx = inp.scale_x
+        _require_cuda(sx, "scale_x")
+        if sx.dtype != torch.float32 or tuple(sx.shape) != (n_tok, n_layers):
+            raise ValueError("scale_x must be float32 [n_tokens, n_layers]")
+        d.scale_x, d.sx_tstride, d.sx_lstride = sx.data_ptr(), sx.stride(0), sx.stride(1)
+
+        def per_layer(seq, m):
+            out = []
+            for l in range(n_layers):
+                e = seq[l] if seq is not None and l < len(seq) and seq[l] is not None else None
+                t = e[m] if e is not None else None
+                if t is not None and t.numel() > 0:
+                    _require_cuda(t, "scale/bias")
+                    if t.dtype != torch.float32 or t.numel() != kv or not t.is_contiguous():
+                        raise ValueError(f"per-channel scales and biases must be contiguous float32 [{kv}]")
+                    out.append(t.data_ptr())
+                else:
+                    out.append(None)
+            return pp(_ptrs(out))
+
+        swk = (ctypes.c_float * n_layers)()
+        swv = (ctypes.c_float * n_layers)()
+        for l in range(n_layers):
+            if inp.per_tensor and l < len(inp.per_tensor) and inp.per_tensor[l] is not None:
+                swk[l], swv[l] = float(inp.per_tensor[l][0]), float(inp.per_tensor[l][1])
+        d.sw_k = ctypes.cast(swk, ctypes.POINTER(ctypes.c_float))
+        d.sw_v = ctypes.cast(swv, ctypes.POINTER(ctypes.c_float))
+        d.ch_k, d.ch_v = per_layer(inp.per_channel, 0), per_layer(inp.per_channel, 1)
+        d.bias_k, d.bias_v = per_layer(inp.biases, 0), per_layer(inp.biases, 1)
+        keep += [swk, swv]
+        r = inp.rope or RopeConfig()
+        d.rope_theta = float(r.theta)
+        d.rope_scaling = {"llama3": _lib.VC_ROPE_LLAMA3, "linear": _lib.VC_ROPE_LINEAR}.get(r.scaling or "",
+                                                                                          _lib.VC_ROPE_NONE)
+        d.rope_original_max_position_embeddings = int(r.original_max_position_embeddings)
+        d.rope_factor, d.rope_low_freq_factor = float(r.factor), float(r.low_freq_factor)
+        d.rope_high_freq_factor = float(r.high_freq_factor)
+    if k_out is None:
+        k_out = ctx.empty(n_layers, n_tok, kv, dtype=torch.float64)
+    if v_out is None:
+        v_out = ctx.empty(n_layers, n_tok, kv, dtype=torch.float64)
+    for o in (k_out, v_out):
+        if o.dtype != torch.float64 or tuple(o.shape) != (n_layers, n_tok, kv) or not o.is_contiguous():
+            raise ValueError("outputs must be contiguous float64 [n_layers, n_tokens, kv_dim]")
+    check(lib().vc_kv_transcript(ctx.handle, ctypes.byref(d), ctypes.c_void_p(k_out.data_ptr()),
+                                 ctypes.c_void_p(v_out.data_ptr())))
+    return k_out, v_out
+
+
+def kv_transcript_view(k: torch.Tensor, v: torch.Tensor, layer_base: int = 0) -> KvCacheView:
+    """The committed transcript as a one-sequence contiguous KV view (f64
+    rows) for :func:`kv_commit` and :func:`kv_open`."""
+    n_layers, n_tok, kv = k.shape
+    return KvCacheView(k_layers=[k[l].view(n_tok, 1, kv) for l in range(n_layers)],
+                       v_layers=[v[l].view(n_tok, 1, kv) for l in range(n_layers)],
+                       seq_lens=[n_tok], layer_base=layer_base)

@@ -79,6 +79,9 @@ struct vc_ctx {
   cudaEvent_t staged = nullptr;     // the last staging copy has been read
   bool staged_pending = false;
   int n_sm = 0;
+  double* rope = nullptr;           // device (cos, sin) table of the last RoPE frequencies
+  int64_t rope_rows = 0;            // positions held
+  std::vector<double> rope_inv;     // the frequencies it was built for
 };
 
 namespace {
@@ -87,8 +90,8 @@ namespace {
 // device (stream-ordered) and returns the device base.
 struct Stager {
   std::vector<char> img;
-  size_t add(const void* p, size_t n) {
-    const size_t off = align_up(img.size(), 16);
+  size_t add(const void* p, size_t n, size_t align = 16) {
+    const size_t off = align_up(img.size(), align);
     img.resize(off + n);
     if (n) std::memcpy(img.data() + off, p, n);
     return off;
@@ -262,6 +265,7 @@ vc_status vc_ctx_destroy(vc_ctx* c) {
   if (c->dargs) cudaFree(c->dargs);
   if (c->pinned) cudaFreeHost(c->pinned);
   if (c->staged) cudaEventDestroy(c->staged);
+  if (c->rope) cudaFree(c->rope);
   delete c;
   return VC_OK;
 }
@@ -284,6 +288,7 @@ vc_status vc_ctx_sync(vc_ctx* c, int32_t timeout_ms) {
   VC_CUDA(cudaMemcpy(&flag, c->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (flag) {
     VC_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+    if (flag == 2) return fail(VC_ETIMEDOUT, "a bounded wait inside a kernel ran out (results of that launch are void)");
     return fail(VC_ERANGE, "a K/V row addressed through the block table lies outside cache_elems");
   }
   return VC_OK;
@@ -678,8 +683,40 @@ vc_status vc_io_chain(vc_ctx* c, int32_t n_seqs, const int64_t* tok_off, const u
   vc_status r = upload(c, st, &dev);
   if (r) return r;
   const cudaError_t e = launch_io_chain(n_seqs, reinterpret_cast<const int64_t*>(dev + o), leaves_dev, token_ids_dev,
-                                        prompt_hash_dev, io_dev, c->stream);
+                                        prompt_hash_dev, io_dev, nullptr, c->stream);
   if (e != cudaSuccess) return fail(VC_ECUDA, "vc_io_chain launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
+vc_status vc_io_extend(vc_ctx* c, int32_t n_seqs, const int64_t* tok_off, const uint8_t* leaves_dev,
+                       const uint32_t* token_ids_dev, uint8_t* prev_io_dev, uint8_t* io_dev) {
+  if (!c || !tok_off || !prev_io_dev || (tok_off[n_seqs] > tok_off[0] && (!leaves_dev || !token_ids_dev || !io_dev)))
+    return fail(VC_EINVAL, "vc_io_extend: NULL argument");
+  if (n_seqs < 1) return fail(VC_EINVAL, "vc_io_extend: n_seqs must be >= 1");
+  for (int s = 0; s < n_seqs; ++s)
+    if (tok_off[s] < 0 || tok_off[s + 1] < tok_off[s]) return fail(VC_EINVAL, "vc_io_extend: tok_off not ascending at %d", s);
+  for (const void* p : {(const void*)leaves_dev, (const void*)prev_io_dev, (const void*)io_dev})
+    if (p && reinterpret_cast<uintptr_t>(p) % 16) return fail(VC_EINVAL, "vc_io_extend: digest arrays must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  Stager st;
+  const size_t o = st.add(tok_off, sizeof(int64_t) * (n_seqs + 1));
+  char* dev = nullptr;
+  vc_status r = upload(c, st, &dev);
+  if (r) return r;
+  const cudaError_t e = launch_io_chain(n_seqs, reinterpret_cast<const int64_t*>(dev + o), leaves_dev, token_ids_dev,
+                                        nullptr, io_dev, prev_io_dev, c->stream);
+  if (e != cudaSuccess) return fail(VC_ECUDA, "vc_io_extend launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
+vc_status vc_io_genesis(vc_ctx* c, int32_t n, const uint8_t* prompt_hash_dev, uint8_t* out_dev) {
+  if (!c || (n > 0 && (!prompt_hash_dev || !out_dev))) return fail(VC_EINVAL, "vc_io_genesis: NULL argument");
+  if (n < 0) return fail(VC_EINVAL, "vc_io_genesis: negative count");
+  if (n > 0 && reinterpret_cast<uintptr_t>(out_dev) % 16) return fail(VC_EINVAL, "vc_io_genesis: out_dev not 16-byte aligned");
+  if (n == 0) return VC_OK;
+  DeviceGuard g(c->device);
+  const cudaError_t e = launch_tagged_hash(n, 2, prompt_hash_dev, nullptr, 32, out_dev, c->stream);
+  if (e != cudaSuccess) return fail(VC_ECUDA, "vc_io_genesis launch: %s", cudaGetErrorString(e));
   return VC_OK;
 }
 
@@ -713,6 +750,106 @@ vc_status vc_seed_commitment(vc_ctx* c, int32_t n, const uint8_t* seeds_dev, uin
 }
 
 // ------------------------------------------------------- measurement aid
+
+// ------------------------------------------------------------ KV transcript
+
+vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, double* v_out) {
+  if (!c || !d) return fail(VC_EINVAL, "vc_kv_transcript: NULL argument");
+  if (d->n_tokens < 0 || d->n_layers < 1 || d->n_kv_heads < 1)
+    return fail(VC_EINVAL, "vc_kv_transcript: n_tokens >= 0, n_layers and n_kv_heads >= 1 required");
+  if (d->hidden < 16 || d->hidden % 16) return fail(VC_EINVAL, "vc_kv_transcript: hidden %d must be a positive multiple of 16", d->hidden);
+  if (d->head_dim < 2 || d->head_dim % 2 || d->head_dim > 256)
+    return fail(VC_EINVAL, "vc_kv_transcript: head_dim %d must be even and <= 256", d->head_dim);
+  const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
+  if (kv > (int64_t(1) << 24)) return fail(VC_EINVAL, "vc_kv_transcript: kv_dim too large");
+  if (d->n_tokens == 0) return VC_OK;
+  if (!k_out || !v_out) return fail(VC_EINVAL, "vc_kv_transcript: NULL output");
+  if (d->x_row_stride < d->hidden || d->x_row_stride % 16)
+    return fail(VC_EINVAL, "vc_kv_transcript: x_row_stride must be >= hidden and a multiple of 16");
+  if (!d->x_layers || !d->wk_layers || !d->wv_layers) return fail(VC_EINVAL, "vc_kv_transcript: NULL layer table");
+  if (d->use_rope && !d->scale_x) return fail(VC_EINVAL, "vc_kv_transcript: scale_x is NULL");
+  if (reinterpret_cast<uintptr_t>(k_out) % 16 || reinterpret_cast<uintptr_t>(v_out) % 16)
+    return fail(VC_EINVAL, "vc_kv_transcript: outputs must be 16-byte aligned");
+  for (int l = 0; l < d->n_layers; ++l) {
+    const void* p[3] = {d->x_layers[l], d->wk_layers[l], d->wv_layers[l]};
+    for (const void* q : p)
+      if (!q || reinterpret_cast<uintptr_t>(q) % 16)
+        return fail(VC_EINVAL, "vc_kv_transcript: x/Wk/Wv pointer of layer %d is NULL or not 16-byte aligned", l);
+  }
+  DeviceGuard g(c->device);
+
+  // (cos, sin) table: built once per frequency set on the host (C library cos/sin)
+  if (d->use_rope) {
+    const std::vector<double> inv =
+        kvt_inv_freq(d->head_dim, d->rope_theta, d->rope_scaling, d->rope_factor, d->rope_low_freq_factor,
+                     d->rope_high_freq_factor, d->rope_original_max_position_embeddings);
+    const bool same = inv.size() == c->rope_inv.size() &&
+                      std::memcmp(inv.data(), c->rope_inv.data(), inv.size() * sizeof(double)) == 0;
+    if (!same || c->rope_rows < d->n_tokens) {
+      const int64_t rows = std::max<int64_t>(d->n_tokens, same ? 2 * c->rope_rows : 0);
+      std::vector<double> tab(size_t(rows) * inv.size() * 2);
+      kvt_rope_table(inv, rows, tab.data());
+      VC_CUDA(cudaStreamSynchronize(c->stream));
+      if (c->rope) cudaFree(c->rope);
+      c->rope = nullptr;
+      c->rope_rows = 0;
+      c->rope_inv.clear();
+      if (cudaMalloc(&c->rope, tab.size() * sizeof(double)) != cudaSuccess)
+        return fail(VC_ENOMEM, "vc_kv_transcript: RoPE table of %zu bytes", tab.size() * sizeof(double));
+      VC_CUDA(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(double), cudaMemcpyHostToDevice));
+      c->rope_rows = rows;
+      c->rope_inv = inv;
+    }
+  }
+
+  // tensor maps (x_attn, Wk, Wv per layer) and per-layer scale/bias tables
+  std::vector<CUtensorMap> maps(size_t(d->n_layers) * 3);
+  std::vector<KvtLayer> layers(d->n_layers);
+  for (int l = 0; l < d->n_layers; ++l) {
+    int r = kvt_encode_map(&maps[3 * l], d->x_layers[l], d->hidden, d->n_tokens, d->x_row_stride, 128);
+    if (!r) r = kvt_encode_map(&maps[3 * l + 1], d->wk_layers[l], d->hidden, kv, d->hidden, 256);
+    if (!r) r = kvt_encode_map(&maps[3 * l + 2], d->wv_layers[l], d->hidden, kv, d->hidden, 256);
+    if (r) return fail(VC_ECUDA, "vc_kv_transcript: cuTensorMapEncodeTiled failed (%d) for layer %d", r, l);
+    KvtLayer& L = layers[l];
+    std::memset(&L, 0, sizeof(L));
+    L.ch[0] = d->ch_k ? d->ch_k[l] : nullptr;
+    L.ch[1] = d->ch_v ? d->ch_v[l] : nullptr;
+    L.bias[0] = d->bias_k ? d->bias_k[l] : nullptr;
+    L.bias[1] = d->bias_v ? d->bias_v[l] : nullptr;
+    L.sw[0] = d->sw_k ? d->sw_k[l] : 0.0f;
+    L.sw[1] = d->sw_v ? d->sw_v[l] : 0.0f;
+  }
+  Stager st;
+  const size_t om = st.add(maps.data(), maps.size() * sizeof(CUtensorMap), 128);
+  const size_t ol = st.add(layers.data(), layers.size() * sizeof(KvtLayer));
+  char* dev = nullptr;
+  vc_status r = upload(c, st, &dev);
+  if (r) return r;
+
+  KvtArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.maps = reinterpret_cast<const CUtensorMap*>(dev + om);
+  a.layers = reinterpret_cast<const KvtLayer*>(dev + ol);
+  a.scale_x = d->scale_x;
+  a.sx_t = d->sx_tstride;
+  a.sx_l = d->sx_lstride;
+  a.rope = d->use_rope ? reinterpret_cast<const double2*>(c->rope) : nullptr;
+  a.out[0] = k_out;
+  a.out[1] = v_out;
+  a.n_tokens = d->n_tokens;
+  a.hidden = d->hidden;
+  a.kv_dim = int32_t(kv);
+  a.head_dim = d->head_dim;
+  a.tile_cols = (256 / d->head_dim) * d->head_dim;
+  a.tiles_per_mat = int32_t((kv + a.tile_cols - 1) / a.tile_cols);
+  a.use_rope = d->use_rope != 0;
+  a.err = c->err;
+  if (int64_t(2) * a.tiles_per_mat > 0x7FFFFFFF || (d->n_tokens + 127) / 128 > 65535 || d->n_layers > 65535)
+    return fail(VC_EINVAL, "vc_kv_transcript: grid too large");
+  const cudaError_t e = launch_kv_transcript(a, d->n_layers, c->stream);
+  if (e != cudaSuccess) return fail(VC_ECUDA, "vc_kv_transcript launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
 
 vc_status vc_int_peak(vc_ctx* c, int32_t variant, int64_t iters, double* ops_per_s) {
   if (!c || !ops_per_s || iters < 1 || variant < 0 || variant > 3) return fail(VC_EINVAL, "vc_int_peak: bad argument");

@@ -14,6 +14,7 @@ __device__ const char kTagLp[] = "vi-retained-lp-v1";
 __device__ const char kTagLogits[] = "vi-retained-logits-v1";
 __device__ const char kTagPrompt[] = "vi-prompt-v1";
 __device__ const char kTagSeed[] = "vi-seed-v1";
+__device__ const char kTagGenesis[] = "vi-io-genesis-v4";
 
 // One thread per token: hash_retained_state_direct (merkle.rs:144-161), then
 // the optional wraps of hash_retained_with_captured_logits (merkle.rs:170-241).
@@ -85,12 +86,17 @@ __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(TraceArgs a) 
 // the per-token time (~3.5 us on B200).  Computing each token's first 11
 // rounds ahead in parallel, moving adds to the FMA pipe, or shortening the
 // round's dependency chain with extra adds were measured and did not help.
+// prev_io (optional): the chain continues from prev_io[s] instead of the
+// genesis, and the last value is written back there (online extension).
 __global__ void io_chain_kernel(int n_seqs, const int64_t* tok_off, const uint8_t* leaves,
-                                const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io) {
+                                const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io,
+                                uint8_t* prev_io) {
   const int s = blockIdx.x;   // one sequence per CTA of one warp; lane 0 runs the chain
   if (s >= n_seqs || threadIdx.x != 0) return;
   uint32_t prev[8];
-  {
+  if (prev_io) {
+    load_digest(prev_io + int64_t(s) * 32, prev);
+  } else {
     uint32_t ph[8];
     load_digest(prompt_hash + int64_t(s) * 32, ph);
     uint32_t w[16] = {0x76692d69u, 0x6f2d6765u, 0x6e657369u, 0x732d7634u,  // "vi-io-genesis-v4"
@@ -100,7 +106,7 @@ __global__ void io_chain_kernel(int n_seqs, const int64_t* tok_off, const uint8_
     compress(prev, w);
   }
   const int64_t t0 = tok_off[s], t1 = tok_off[s + 1];
-  if (t0 >= t1) return;
+  if (t0 >= t1) return;   // nothing appended: prev_io keeps its value
   uint32_t leaf[8], tok;
   load_digest(leaves + t0 * 32, leaf);
   tok = token_ids[t0];
@@ -125,11 +131,14 @@ __global__ void io_chain_kernel(int n_seqs, const int64_t* tok_off, const uint8_
     for (int i = 0; i < 8; ++i) { prev[i] = st[i]; leaf[i] = nleaf[i]; }
     tok = ntok;
   }
+  if (prev_io) store_digest(prev_io + int64_t(s) * 32, prev);
 }
 
 // SHA256(tag || data_i), one thread per message.  tag 0: "vi-prompt-v1"
 // over [off[i], off[i+1]) (hash_prompt, merkle.rs:561-566); tag 1:
-// "vi-seed-v1" over 32 bytes at data + 32 i (hash_seed, merkle.rs:553-558).
+// "vi-seed-v1" over 32 bytes at data + 32 i (hash_seed, merkle.rs:553-558);
+// tag 2: "vi-io-genesis-v4" over a 32-byte prompt hash (io_genesis_v4,
+// merkle.rs:572-577).
 __global__ void __launch_bounds__(kTraceThreads) tagged_hash_kernel(int n, int tag, const uint8_t* data,
                                                                      const int64_t* off, int64_t fixed_len,
                                                                      uint8_t* out) {
@@ -140,7 +149,9 @@ __global__ void __launch_bounds__(kTraceThreads) tagged_hash_kernel(int n, int t
   const int64_t len = off ? off[i + 1] - off[i] : fixed_len;
   Sha256Stream<kTraceThreads> s;
   s.init(sbuf + threadIdx.x);
-  if (tag == 0) s.put_tag(kTagPrompt, 12); else s.put_tag(kTagSeed, 10);
+  if (tag == 0) s.put_tag(kTagPrompt, 12);
+  else if (tag == 1) s.put_tag(kTagSeed, 10);
+  else s.put_tag(kTagGenesis, 16);
   if (len > 0) s.put_array(data + b, len);
   s.finish();
   store_digest(out + int64_t(i) * 32, s.h);
@@ -153,8 +164,9 @@ cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
-                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, cudaStream_t s) {
-  io_chain_kernel<<<n_seqs, 32, 0, s>>>(n_seqs, tok_off_dev, leaves, token_ids, prompt_hash, io);
+                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, uint8_t* prev_io,
+                            cudaStream_t s) {
+  io_chain_kernel<<<n_seqs, 32, 0, s>>>(n_seqs, tok_off_dev, leaves, token_ids, prompt_hash, io, prev_io);
   return cudaGetLastError();
 }
 

@@ -1,7 +1,9 @@
 // Internal declarations shared by the CUDA translation units of libvcommit.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <vector>
 
 namespace vc {
 
@@ -97,12 +99,43 @@ struct TraceArgs {
 };
 cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s);
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
-                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, cudaStream_t s);
+                            const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, uint8_t* prev_io,
+                            cudaStream_t s);
 cudaError_t launch_tagged_hash(int n, int tag, const uint8_t* data, const int64_t* off_dev,
                                int64_t fixed_len, uint8_t* out, cudaStream_t s);
 
 // api.cu: record the calling thread's error text (read by vc_last_error).
 int32_t set_error(int32_t status, const char* fmt, ...);
+
+// kv_transcript.cu
+struct KvtLayer {
+  const float* ch[2];     // per-channel weight scales of Wk, Wv ([kv_dim]) or nullptr
+  const float* bias[2];   // K, V projection biases ([kv_dim]) or nullptr
+  float sw[2];            // per-tensor weight scales (0 when absent)
+  int32_t pad_[2];
+};
+
+struct KvtArgs {
+  const CUtensorMap* maps;     // [n_layers][3]: x_attn, Wk, Wv (64-byte aligned, device)
+  const KvtLayer* layers;      // [n_layers]
+  const float* scale_x;        // scale_x_attn of (t, l) at t * sx_t + l * sx_l
+  int64_t sx_t, sx_l;
+  const double2* rope;         // [n_tokens][head_dim / 2] (cos, sin), or nullptr (toy path)
+  double* out[2];              // K, V: [n_layers][n_tokens][kv_dim]
+  int32_t n_tokens, hidden, kv_dim, head_dim;
+  int32_t tile_cols;           // channels stored per tile: whole heads, <= 256
+  int32_t tiles_per_mat;
+  int32_t use_rope;
+  int* err;                    // set to 2 when a bounded wait ran out
+};
+int kvt_group_width(int head_dim);
+size_t kvt_smem_bytes();
+std::vector<double> kvt_inv_freq(int head_dim, double theta, int scaling_type, double factor, double low_ff,
+                                 double high_ff, int64_t orig_max_pos);
+void kvt_rope_table(const std::vector<double>& inv, int64_t n_pos, double* out);
+int kvt_encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t row_stride,
+                   int box_rows);
+cudaError_t launch_kv_transcript(const KvtArgs& a, int n_layers, cudaStream_t s);
 
 // int_peak.cu
 cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,

@@ -224,6 +224,20 @@ VC_API vc_status vc_io_chain(vc_ctx* ctx, int32_t n_seqs, const int64_t* tok_off
                       const uint8_t* leaves_dev, const uint32_t* token_ids_dev,
                       const uint8_t* prompt_hash_dev, uint8_t* io_dev);
 
+/*
+ * Online extension of IO chains (the same loop as vc_io_chain, resumed):
+ * sequence s appends the tokens [tok_off[s], tok_off[s+1]) -- leaves_dev,
+ * token_ids_dev and io_dev indexed by token as in vc_io_chain -- starting
+ * from prev_io_dev[s] (its last io value, or its genesis), and
+ * prev_io_dev[s] receives the new last value.  A sequence with no tokens
+ * keeps its value.  prev_io_dev: DEVICE [n_seqs][32].
+ */
+VC_API vc_status vc_io_extend(vc_ctx* ctx, int32_t n_seqs, const int64_t* tok_off, const uint8_t* leaves_dev,
+                              const uint32_t* token_ids_dev, uint8_t* prev_io_dev, uint8_t* io_dev);
+
+/* io_genesis_v4 (merkle.rs:572-577) of n prompt hashes: DEVICE [n][32] -> [n][32]. */
+VC_API vc_status vc_io_genesis(vc_ctx* ctx, int32_t n, const uint8_t* prompt_hash_dev, uint8_t* out_dev);
+
 /* hash_prompt (merkle.rs:561-566) of n prompts; prompt i is the bytes
  * [off[i], off[i+1]) of prompts_dev.  off: HOST [n + 1]; out: DEVICE [n][32]. */
 VC_API vc_status vc_prompt_hash(vc_ctx* ctx, int32_t n, const uint8_t* prompts_dev,
@@ -284,6 +298,55 @@ VC_API int32_t vc_tree_set_count(const vc_tree_set* trees);
 VC_API vc_status vc_tree_nodes(const vc_tree_set* trees, int32_t tree, const uint8_t** nodes_dev,
                         int64_t* n_leaves, int64_t* padded_size);
 VC_API vc_status vc_tree_set_free(vc_tree_set* trees);
+
+/* ------------------------------------------------------------ KV transcript */
+
+/* Rope scaling of ModelConfig (crates/verilm-core/src/constants.rs:126-156). */
+#define VC_ROPE_NONE 0
+#define VC_ROPE_LLAMA3 1
+#define VC_ROPE_LINEAR 2
+
+typedef struct vc_kvt_desc {
+    int32_t n_tokens;        /* positions 0..n_tokens-1 (token order of captured_x_attn) */
+    int32_t n_layers;
+    int32_t hidden;          /* hidden_dim: multiple of 16 */
+    int32_t n_kv_heads;
+    int32_t head_dim;        /* d_head: even, <= 256 */
+    int32_t use_rope;        /* 0: toy path (clamp to i8, lib.rs:307-316); 1: dequant + bias + RoPE */
+    const int8_t* const* x_layers;   /* HOST [n_layers] DEVICE: row t of layer l at x_layers[l] + t * x_row_stride */
+    int64_t x_row_stride;            /* bytes, multiple of 16, >= hidden */
+    const int8_t* const* wk_layers;  /* HOST [n_layers] DEVICE [kv_dim][hidden] row-major (Wk) */
+    const int8_t* const* wv_layers;  /* HOST [n_layers] DEVICE [kv_dim][hidden] row-major (Wv) */
+    const float* scale_x;            /* DEVICE: scale_x_attn of (t, l) at scale_x[t * sx_tstride + l * sx_lstride] */
+    int64_t sx_tstride, sx_lstride;
+    const float* sw_k;               /* HOST [n_layers] per-tensor scales of Wk, or NULL (0.0) */
+    const float* sw_v;               /* HOST [n_layers] per-tensor scales of Wv, or NULL (0.0) */
+    const float* const* ch_k;        /* HOST [n_layers] of DEVICE [kv_dim] per-channel scales, or NULL;
+                                        a NULL entry falls back to the per-tensor scale */
+    const float* const* ch_v;
+    const float* const* bias_k;      /* HOST [n_layers] of DEVICE [kv_dim] biases, or NULL / NULL entries */
+    const float* const* bias_v;
+    double rope_theta;
+    int32_t rope_scaling;            /* VC_ROPE_* */
+    int32_t rope_original_max_position_embeddings;
+    double rope_factor, rope_low_freq_factor, rope_high_freq_factor;
+} vc_kvt_desc;
+
+/*
+ * verilm_prover::compute_kv_transcript (crates/verilm-prover/src/lib.rs:207-329):
+ * the committed KV values from captured x_attn and the Wk/Wv weights, on the
+ * tensor cores.  k_acc = Wk x_attn, v_acc = Wv x_attn (exact i32, matmul.rs:12-22);
+ * use_rope: per-channel ((acc * cw[c]) * sx, rope.rs:124-138) when the layer has
+ * a per-channel table, else acc * (sw * sx) (rope.rs:107-112); + bias; K rotated
+ * per head with scaled_inv_freq (constants.rs:253-297) and the C library's
+ * cos/sin (rope.rs:38-60, 88-100).  Every f64 operation is rounded on its own.
+ * k_out_dev / v_out_dev: DEVICE f64 [n_layers][n_tokens][kv_dim] (16-byte
+ * aligned): KvEntry.k_roped / v_deq of (layer, position), ready for
+ * vc_kv_commit with VC_DTYPE_F64 and stride_row = kv_dim.
+ * Weights and x_attn base pointers must be 16-byte aligned (VC_EINVAL).
+ * A wait that runs out inside the kernel is reported by vc_ctx_sync as VC_ETIMEDOUT.
+ */
+VC_API vc_status vc_kv_transcript(vc_ctx* ctx, const vc_kvt_desc* desc, double* k_out_dev, double* v_out_dev);
 
 /* --------------------------------------------------------- measurement aid */
 

@@ -427,3 +427,147 @@ def packed_token_layers(packed_a: bytes, packed_scales: np.ndarray, n_layers: in
 def sha256_blocks(msg_len: int) -> int:
     """FIPS 180-4 block count for a message of ``msg_len`` bytes."""
     return (msg_len + 9 + 63) // 64
+
+
+# ---------------------------------------------------------------------------
+# KV transcript from captured x_attn and the Wk/Wv weights:
+# crates/verilm-prover/src/lib.rs:207-329 (compute_kv_transcript)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class RopeScaling:
+    """``RopeScaling`` (crates/verilm-core/src/constants.rs:126-137)."""
+    rope_type: str = "llama3"
+    factor: float = 8.0
+    low_freq_factor: float = 1.0
+    high_freq_factor: float = 4.0
+    original_max_position_embeddings: int = 8192
+
+
+def scaled_inv_freq(d_head: int, rope_theta: float, scaling: Optional[RopeScaling] = None) -> List[float]:
+    """``ModelConfig::scaled_inv_freq`` (constants.rs:253-297), f64 throughout.
+
+    ``math.pow`` is the C library's ``pow``, the function Rust's ``f64::powf``
+    calls on Linux, so the frequencies are the reference's bit for bit.
+    """
+    import math
+    half = d_head // 2
+    base = [1.0 / math.pow(rope_theta, float(2 * k) / float(d_head)) for k in range(half)]
+    if scaling is None:
+        return base
+    if scaling.rope_type == "llama3":
+        old_ctx = float(scaling.original_max_position_embeddings)
+        low_wl = old_ctx / scaling.low_freq_factor
+        high_wl = old_ctx / scaling.high_freq_factor
+        out = []
+        for f in base:
+            wl = 2.0 * math.pi / f
+            if wl < high_wl:
+                out.append(f)
+            elif wl > low_wl:
+                out.append(f / scaling.factor)
+            else:
+                smooth = (old_ctx / wl - scaling.low_freq_factor) / (scaling.high_freq_factor - scaling.low_freq_factor)
+                out.append(f * ((1.0 - smooth) / scaling.factor + smooth))
+        return out
+    if scaling.rope_type == "linear":
+        return [f / scaling.factor for f in base]
+    return base
+
+
+def rope_cos_sin(n_positions: int, inv_freq: Sequence[float]):
+    """cos/sin of ``position as f64 * inv_freq[i]`` (rope.rs:48-52), with the
+    C library's ``cos``/``sin`` (what Rust's ``f64::cos``/``sin`` call)."""
+    import math
+    half = len(inv_freq)
+    c = np.empty((n_positions, half), np.float64)
+    s = np.empty((n_positions, half), np.float64)
+    for p in range(n_positions):
+        for i, f in enumerate(inv_freq):
+            a = float(p) * f
+            c[p, i] = math.cos(a)
+            s[p, i] = math.sin(a)
+    return c, s
+
+
+def matmul_i32(w: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """``matmul_i32`` (crates/verilm-core/src/matmul.rs:12-22) for a batch of
+    vectors: ``x [n][cols] i8`` times ``w [rows][cols] i8`` -> ``[n][rows] i32``.
+
+    Computed as an f64 matrix product: every product and every partial sum is
+    an integer below 2^53 in magnitude, so the f64 result is exact whatever the
+    summation order, and equals the i32 sum while that does not overflow.
+    """
+    acc = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
+    return acc.astype(np.int64).astype(np.int32)
+
+
+def compute_kv_transcript(x_attn: np.ndarray, wk: Sequence[np.ndarray], wv: Sequence[np.ndarray],
+                          scale_x: np.ndarray, n_kv_heads: int, d_head: int,
+                          per_tensor=None, per_channel=None, biases=None,
+                          rope_theta: float = 10000.0, rope_scaling: Optional[RopeScaling] = None):
+    """``compute_kv_transcript`` (prover/src/lib.rs:207-329).
+
+    x_attn: ``[n_tokens][n_layers][hidden]`` i8 (captured ``x_attn``, token
+    order = position); wk/wv: per layer ``[kv_dim][hidden]`` i8; scale_x:
+    ``[n_tokens][n_layers]`` f32 (``scale_x_attn``).  per_tensor: per layer
+    ``(sw_k, sw_v)`` f32 or None; per_channel: per layer ``(cw_k, cw_v)``
+    ``[kv_dim]`` f32 arrays (either may be None: that layer uses its per-tensor
+    scale, 0.0 when absent, lib.rs:244-279); biases: per layer ``(b_k, b_v)``
+    ``[kv_dim]`` f32 or None (lib.rs:283-302).  With neither scale list the
+    toy path applies: clamp to i8, as f64 (lib.rs:307-316).
+
+    Returns ``k_roped, v_deq`` as ``[n_layers][n_tokens][kv_dim]`` f64.
+    Arithmetic order follows rope.rs exactly: per-tensor ``acc * (sw*sx)``
+    (rope.rs:107-112), per-channel ``(acc*sw[c])*sx`` (rope.rs:124-138), then
+    ``+ bias``, then RoPE per head ``h[i]c - h[i+half]s``, ``h[i+half]c + h[i]s``
+    (rope.rs:38-60, 88-100); numpy elementwise f64 ops round each step, like
+    Rust's (no fused multiply-add).
+    """
+    x_attn = np.asarray(x_attn, np.int8)
+    n_tok, n_layers, hidden = x_attn.shape
+    kv_dim = n_kv_heads * d_head
+    use_rope = bool(per_tensor) or bool(per_channel)
+    scale_x = np.asarray(scale_x, np.float32)
+    k_out = np.empty((n_layers, n_tok, kv_dim), np.float64)
+    v_out = np.empty((n_layers, n_tok, kv_dim), np.float64)
+    if use_rope:
+        inv = scaled_inv_freq(d_head, rope_theta, rope_scaling)
+        cos, sin = rope_cos_sin(n_tok, inv)
+    half = d_head // 2
+    for l in range(n_layers):
+        x = x_attn[:, l, :]
+        k_acc = matmul_i32(wk[l], x)
+        v_acc = matmul_i32(wv[l], x)
+        if not use_rope:
+            k_out[l] = np.clip(k_acc, -128, 127).astype(np.float64)
+            v_out[l] = np.clip(v_acc, -128, 127).astype(np.float64)
+            continue
+        sx = scale_x[:, l].astype(np.float64)[:, None]
+        vals = []
+        for m, acc in ((0, k_acc), (1, v_acc)):
+            ch = None
+            if per_channel and l < len(per_channel) and per_channel[l] is not None \
+                    and per_channel[l][m] is not None and len(per_channel[l][m]) > 0:
+                ch = np.asarray(per_channel[l][m], np.float32).astype(np.float64)
+            if ch is not None:
+                f = (acc.astype(np.float64) * ch[None, :]) * sx
+            else:
+                sw = 0.0
+                if per_tensor and l < len(per_tensor) and per_tensor[l] is not None:
+                    sw = float(np.float32(per_tensor[l][m]))
+                f = acc.astype(np.float64) * (sw * sx)
+            if biases and l < len(biases) and biases[l] is not None and biases[l][m] is not None \
+                    and len(biases[l][m]) > 0:
+                f = f + np.asarray(biases[l][m], np.float32).astype(np.float64)[None, :]
+            vals.append(f)
+        k, v = vals
+        kr = np.empty_like(k)
+        for h in range(n_kv_heads):
+            lo = k[:, h * d_head:h * d_head + half]
+            hi = k[:, h * d_head + half:(h + 1) * d_head]
+            kr[:, h * d_head:h * d_head + half] = lo * cos - hi * sin
+            kr[:, h * d_head + half:(h + 1) * d_head] = hi * cos + lo * sin
+        k_out[l] = kr
+        v_out[l] = v
+    return k_out, v_out

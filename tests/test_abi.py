@@ -49,7 +49,8 @@ def _c_layout(struct, fields):
     return [int(x) for x in out]
 
 
-@pytest.mark.parametrize("cls,cname", [(_lib.KvDesc, "vc_kv_desc"), (_lib.TraceDesc, "vc_trace_desc")])
+@pytest.mark.parametrize("cls,cname", [(_lib.KvDesc, "vc_kv_desc"), (_lib.TraceDesc, "vc_trace_desc"),
+                                      (_lib.KvtDesc, "vc_kvt_desc")])
 def test_struct_layouts_match_header(cls, cname):
     names = [f[0] for f in cls._fields_]
     want = _c_layout(cname, names)

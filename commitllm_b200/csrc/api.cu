@@ -834,6 +834,7 @@ vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, doubl
   a.sx_t = d->sx_tstride;
   a.sx_l = d->sx_lstride;
   a.rope = d->use_rope ? reinterpret_cast<const double2*>(c->rope) : nullptr;
+  a.rope_rows = c->rope_rows;
   a.out[0] = k_out;
   a.out[1] = v_out;
   a.n_tokens = d->n_tokens;
@@ -844,9 +845,11 @@ vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, doubl
   a.tiles_per_mat = int32_t((kv + a.tile_cols - 1) / a.tile_cols);
   a.use_rope = d->use_rope != 0;
   a.err = c->err;
-  if (int64_t(2) * a.tiles_per_mat > 0x7FFFFFFF || (d->n_tokens + 127) / 128 > 65535 || d->n_layers > 65535)
-    return fail(VC_EINVAL, "vc_kv_transcript: grid too large");
-  const cudaError_t e = launch_kv_transcript(a, d->n_layers, c->stream);
+  a.m_tiles = (d->n_tokens + 127) / 128;
+  const int64_t n_tiles = int64_t(d->n_layers) * a.m_tiles * 2 * a.tiles_per_mat;
+  if (n_tiles > 0x7FFFFFFF) return fail(VC_EINVAL, "vc_kv_transcript: too many tiles");
+  a.n_tiles = int32_t(n_tiles);
+  const cudaError_t e = launch_kv_transcript(a, c->n_sm, c->stream);
   if (e != cudaSuccess) return fail(VC_ECUDA, "vc_kv_transcript launch: %s", cudaGetErrorString(e));
   return VC_OK;
 }

@@ -4,17 +4,18 @@
 // For every layer l and position t:
 //   k_acc = Wk[l] x_attn[t][l],  v_acc = Wv[l] x_attn[t][l]      (exact i32)
 //   value = dequant(acc) (+ bias), K additionally rotated by RoPE (f64)
-// One CTA computes a 128-position x 256-channel tile of one layer's K or V
-// projection: TMA brings 128-byte K-slices of x_attn (A, 128 rows) and of the
-// weight rows (B, 256 rows) into shared memory (128-byte swizzle), one thread
-// issues tcgen05.mma kind::i8 into a 128 x 256 s32 accumulator in TMEM, and
-// the four warps read it back (one position per thread) for the f64 epilogue.
+// A tile is 128 positions x 256 channels of one layer's K or V projection:
+// TMA brings 128-byte K-slices of x_attn (A, 128 rows) and of the weight rows
+// (B, 256 rows) into shared memory (128-byte swizzle), one thread issues
+// tcgen05.mma kind::i8 into a 128 x 256 s32 accumulator in TMEM, and four
+// epilogue warps read it back (one position per thread) for the f64 values.
 // i8 x i8 products summed in s32 are exact in any order, so the accumulators
 // equal matmul_i32 (crates/verilm-core/src/matmul.rs:12-22).  The epilogue
 // rounds every f64 operation separately (__dmul_rn / __dadd_rn: no fused
 // multiply-add), in the reference's order; cos/sin come from a host table.
 #include <cuda.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -29,20 +30,26 @@ namespace {
 constexpr int kBM = 128;       // positions per tile (TMEM lanes)
 constexpr int kBN = 256;       // accumulator columns per tile
 constexpr int kBK = 128;       // bytes of K per stage (one swizzle row)
-constexpr int kStages = 2;
-constexpr int kThreads = 128;
+constexpr int kStages = 3;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
 constexpr uint32_t kStageA = kBM * kBK;
 constexpr uint32_t kStageB = kBN * kBK;
 constexpr uint32_t kIdesc = tc05::idesc_i8_s32(kBM, kBN);
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
 constexpr int kErrTimeout = 2;
+constexpr int kChunk = 32;                           // output columns per staged chunk
+constexpr uint32_t kStageOut = 2 * 32 * kChunk * 8;  // two [32 rows][32 cols] f64 chunks per epilogue warp
 
 struct Smem {
   uint8_t a[kStages][kStageA];
   uint8_t b[kStages][kStageB];
+  uint8_t out[kEpiWarps][kStageOut];
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t done;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t final_mma;
   uint32_t tmem;
   int32_t abort;
 };
@@ -58,168 +65,300 @@ __device__ __forceinline__ double deq(int32_t acc, int c, const float* ch, doubl
   return f;
 }
 
-// G: columns per TMEM load in the RoPE epilogue = largest power of two <= 32
-// dividing head_dim / 2.
-template <int G>
+__device__ __forceinline__ bool aborted(const Smem& sm) {
+  return *reinterpret_cast<const volatile int32_t*>(&sm.abort) != 0;
+}
+
+__device__ __forceinline__ void set_abort(Smem& sm, int* err) {
+  atomicExch(&sm.abort, 1);
+  atomicExch(err, kErrTimeout);
+}
+
+struct Tile {
+  int layer, m0, mat, c0, nvalid;
+};
+
+// Tile order: channels fastest, then positions, then layers, so that the CTAs
+// working at one time share one layer's weights and one block of x_attn in L2.
+__device__ __forceinline__ Tile tile_of(const KvtArgs& a, int idx) {
+  Tile t;
+  const int n_tiles_n = 2 * a.tiles_per_mat;
+  const int n = idx % n_tiles_n;
+  const int rest = idx / n_tiles_n;
+  t.m0 = (rest % a.m_tiles) * kBM;
+  t.layer = rest / a.m_tiles;
+  t.mat = n / a.tiles_per_mat;
+  t.c0 = (n % a.tiles_per_mat) * a.tile_cols;
+  t.nvalid = min(a.tile_cols, a.kv_dim - t.c0);
+  return t;
+}
+
+// Staged chunk [32 rows][32 cols] f64: row r, 16-byte column pair p lives at
+// r * 256 + ((p ^ (r & 7)) * 16), so both the row-wise writes (one thread per
+// row) and the row-major reads below are free of bank conflicts.
+__device__ __forceinline__ void stage_pair(uint8_t* chunk, int r, int p, double v0, double v1) {
+  *reinterpret_cast<double2*>(chunk + r * 256 + ((p ^ (r & 7)) * 16)) = make_double2(v0, v1);
+}
+
+// Warp-cooperative store of a staged chunk: 16 lanes per row, 256 contiguous
+// bytes per row, rows beyond n_tokens skipped.
+__device__ __forceinline__ void store_chunk(const uint8_t* chunk, int lane, double* out_tile, int64_t row_elems,
+                                            int row0_pos, int n_tokens, int col) {
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const int r = 2 * i + (lane >> 4), p = lane & 15;
+    if (row0_pos + r < n_tokens) {
+      const double2 v = *reinterpret_cast<const double2*>(chunk + r * 256 + ((p ^ (r & 7)) * 16));
+      *reinterpret_cast<double2*>(out_tile + int64_t(r) * row_elems + col + 2 * p) = v;
+    }
+  }
+}
+
+// One persistent CTA per SM walks the tiles (layer, 128 positions, 256 channels
+// of K or V).  Warp 0 streams A/B stages with TMA, warp 1 issues the MMAs into
+// one of two TMEM accumulators, warps 2-5 turn the other accumulator into f64
+// rows, so the epilogue of one tile overlaps the MMAs of the next.
+// FAST: head_dim a multiple of 64 (output chunks of 32 columns, staged in
+// shared memory and stored row-contiguous); otherwise one thread stores its
+// own row, RoPE pairs in groups of G columns.
+template <int G, bool FAST>
 __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArgs a) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int layer = blockIdx.z;
-  const int m0 = blockIdx.y * kBM;
-  const int mat = blockIdx.x / a.tiles_per_mat;                 // 0 = K, 1 = V
-  const int c0 = (blockIdx.x % a.tiles_per_mat) * a.tile_cols;  // first channel of the tile
-  const int nvalid = min(a.tile_cols, a.kv_dim - c0);
   const int nk = (a.hidden + kBK - 1) / kBK;
-  const CUtensorMap* map_a = a.maps + 3 * layer;
-  const CUtensorMap* map_b = a.maps + 3 * layer + 1 + mat;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       tc05::mbar_init(tc05::smem_u32(&sm.full[s]), 1);
       tc05::mbar_init(tc05::smem_u32(&sm.empty[s]), 1);
     }
-    tc05::mbar_init(tc05::smem_u32(&sm.done), 1);
+    for (int b = 0; b < 2; ++b) {
+      tc05::mbar_init(tc05::smem_u32(&sm.acc_full[b]), 1);
+      tc05::mbar_init(tc05::smem_u32(&sm.acc_empty[b]), kEpiWarps);
+    }
+    tc05::mbar_init(tc05::smem_u32(&sm.final_mma), 1);
     sm.abort = 0;
     tc05::mbar_init_fence();
   }
-  if (warp == 0) tc05::tmem_alloc(tc05::smem_u32(&sm.tmem), kBN);
+  if (warp == 0) tc05::tmem_alloc(tc05::smem_u32(&sm.tmem), 2 * kBN);
   tc05::fence_before_sync();
   __syncthreads();
   tc05::fence_after_sync();
   const uint32_t tmem = sm.tmem;
 
-  if (warp == 0 && lane == 0) {
-    // producer: one stage = A[128 x 128 B] + B[256 x 128 B]
-    tc05::tensormap_acquire(map_a);
-    tc05::tensormap_acquire(map_b);
-    int issued = 0;
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kStages, u = kb / kStages;
-      if (u > 0 && !tc05::mbar_wait(tc05::smem_u32(&sm.empty[s]), (u - 1) & 1, kWaitLimitNs)) {
-        ok = false;
-        break;
-      }
-      if (*reinterpret_cast<volatile int32_t*>(&sm.abort)) break;
-      const uint32_t full = tc05::smem_u32(&sm.full[s]);
-      tc05::mbar_arrive_expect_tx(full, kStageA + kStageB);
-      tc05::tma_load_2d(tc05::smem_u32(sm.a[s]), map_a, kb * kBK, m0, full);
-      tc05::tma_load_2d(tc05::smem_u32(sm.b[s]), map_b, kb * kBK, c0, full);
-      issued = kb + 1;
-    }
-    if (!ok) {
-      atomicExch(&sm.abort, 1);
-      atomicExch(a.err, kErrTimeout);
-      // let the copies already issued land before the CTA can exit
-      for (int kb = max(0, issued - kStages); kb < issued; ++kb)
-        tc05::mbar_wait(tc05::smem_u32(&sm.full[kb % kStages]), (kb / kStages) & 1, kWaitLimitNs);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer: 4 x (128 x 256 x 32) per stage
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kStages, u = kb / kStages;
-      if (!tc05::mbar_wait(tc05::smem_u32(&sm.full[s]), u & 1, kWaitLimitNs) ||
-          *reinterpret_cast<volatile int32_t*>(&sm.abort)) {
-        atomicExch(&sm.abort, 1);
-        atomicExch(a.err, kErrTimeout);
-        break;
-      }
-      tc05::fence_after_sync();
-      const uint64_t ad = tc05::sw128_kmajor_desc(tc05::smem_u32(sm.a[s]));
-      const uint64_t bd = tc05::sw128_kmajor_desc(tc05::smem_u32(sm.b[s]));
-#pragma unroll
-      for (int k = 0; k < kBK / 32; ++k)
-        tc05::mma_i8(tmem, ad + 2 * k, bd + 2 * k, kIdesc, (kb | k) != 0);
-      tc05::mma_commit(tc05::smem_u32(&sm.empty[s]));  // frees the stage when these MMAs finish
-    }
-    tc05::mma_commit(tc05::smem_u32(&sm.done));        // all MMAs of this thread finished
-  }
-  __syncwarp();
-
-  // epilogue: thread = TMEM lane = position m0 + 32 warp + lane
-  bool ok = false;
-  if (lane == 0) ok = tc05::mbar_wait(tc05::smem_u32(&sm.done), 0, kWaitLimitNs);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (!ok && lane == 0) atomicExch(a.err, kErrTimeout);
-  tc05::fence_after_sync();
-  ok = ok && !*reinterpret_cast<volatile int32_t*>(&sm.abort);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-
-  if (ok) {
-    const int t = m0 + warp * 32 + lane;
-    const bool valid = t < a.n_tokens;
-    const uint32_t tbase = tmem + (uint32_t(warp * 32) << 16);
-    double* out = (mat ? a.out[1] : a.out[0]) + (int64_t(layer) * a.n_tokens + (valid ? t : 0)) * a.kv_dim + c0;
-    if (!a.use_rope) {
-      // toy path: requantize (clamp to i8), as f64 (lib.rs:307-316; verilm-core/src/lib.rs:22-24)
-      for (int cb = 0; cb < nvalid; cb += 32) {
-        uint32_t r[32];
-        tc05::tmem_ld_wait<32>(tbase + cb, r);
-        if (valid) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (cb + j < nvalid) out[cb + j] = double(min(127, max(-128, int32_t(r[j]))));
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- TMA producer
+      int64_t kb_total = 0;  // stage uses so far (all tiles)
+      bool ok = true;
+      for (int idx = blockIdx.x; idx < a.n_tiles && ok; idx += gridDim.x) {
+        const Tile t = tile_of(a, idx);
+        const CUtensorMap* map_a = a.maps + 3 * t.layer;
+        const CUtensorMap* map_b = a.maps + 3 * t.layer + 1 + t.mat;
+        tc05::tensormap_acquire(map_a);
+        tc05::tensormap_acquire(map_b);
+        for (int kb = 0; kb < nk; ++kb, ++kb_total) {
+          const int s = int(kb_total % kStages);
+          const int64_t u = kb_total / kStages;
+          if (u > 0 && !tc05::mbar_wait(tc05::smem_u32(&sm.empty[s]), uint32_t((u - 1) & 1), kWaitLimitNs)) {
+            set_abort(sm, a.err);
+            ok = false;
+            break;
+          }
+          if (aborted(sm)) { ok = false; break; }
+          const uint32_t full = tc05::smem_u32(&sm.full[s]);
+          tc05::mbar_arrive_expect_tx(full, kStageA + kStageB);
+          tc05::tma_load_2d(tc05::smem_u32(sm.a[s]), map_a, kb * kBK, t.m0, full);
+          tc05::tma_load_2d(tc05::smem_u32(sm.b[s]), map_b, kb * kBK, t.c0, full);
         }
       }
-    } else {
-      const KvtLayer& L = a.layers[layer];
-      const float* ch = mat ? L.ch[1] : L.ch[0];
-      const float* bias = mat ? L.bias[1] : L.bias[0];
-      const double sx = valid ? double(__ldg(a.scale_x + int64_t(t) * a.sx_t + int64_t(layer) * a.sx_l)) : 0.0;
-      const double scale = __dmul_rn(double(mat ? L.sw[1] : L.sw[0]), sx);
-      if (mat == 1) {
-        for (int cb = 0; cb < nvalid; cb += 32) {
-          uint32_t r[32];
-          tc05::tmem_ld_wait<32>(tbase + cb, r);
-          if (valid) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cb + j < nvalid) out[cb + j] = deq(int32_t(r[j]), c0 + cb + j, ch, sx, scale, bias);
+      if (!ok) {
+        // the copies already issued must land before the CTA exits
+        for (int64_t k = kb_total - 1; k >= 0 && k >= kb_total - kStages; --k)
+          tc05::mbar_wait(tc05::smem_u32(&sm.full[k % kStages]), uint32_t((k / kStages) & 1), kWaitLimitNs);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      int64_t kb_total = 0;
+      int it = 0;
+      for (int idx = blockIdx.x; idx < a.n_tiles; idx += gridDim.x, ++it) {
+        const int buf = it & 1, use = it >> 1;
+        if (use > 0 &&
+            !tc05::mbar_wait(tc05::smem_u32(&sm.acc_empty[buf]), uint32_t((use - 1) & 1), kWaitLimitNs)) {
+          set_abort(sm, a.err);
+          break;
+        }
+        if (aborted(sm)) break;
+        tc05::fence_after_sync();
+        const uint32_t d = tmem + uint32_t(buf * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++kb_total) {
+          const int s = int(kb_total % kStages);
+          const int64_t u = kb_total / kStages;
+          if (!tc05::mbar_wait(tc05::smem_u32(&sm.full[s]), uint32_t(u & 1), kWaitLimitNs) || aborted(sm)) {
+            set_abort(sm, a.err);
+            ok = false;
+            break;
           }
+          tc05::fence_after_sync();
+          const uint64_t ad = tc05::sw128_kmajor_desc(tc05::smem_u32(sm.a[s]));
+          const uint64_t bd = tc05::sw128_kmajor_desc(tc05::smem_u32(sm.b[s]));
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k) tc05::mma_i8(d, ad + 2 * k, bd + 2 * k, kIdesc, (kb | k) != 0);
+          tc05::mma_commit(tc05::smem_u32(&sm.empty[s]));  // frees the stage when these MMAs finish
+        }
+        if (!ok) break;
+        tc05::mma_commit(tc05::smem_u32(&sm.acc_full[buf]));  // accumulator ready for the epilogue
+      }
+      // every MMA of this thread has finished before the CTA can free TMEM
+      tc05::mma_commit(tc05::smem_u32(&sm.final_mma));
+      tc05::mbar_wait(tc05::smem_u32(&sm.final_mma), 0, kWaitLimitNs);
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int e = warp - 2;
+    const int quarter = warp & 3;  // this warp may read TMEM lanes 32 * quarter .. + 31
+    uint8_t* stage0 = sm.out[e];
+    uint8_t* stage1 = sm.out[e] + kStageOut / 2;
+    int it = 0;
+    for (int idx = blockIdx.x; idx < a.n_tiles; idx += gridDim.x, ++it) {
+      const int buf = it & 1, use = it >> 1;
+      bool ok = false;
+      if (lane == 0) ok = tc05::mbar_wait(tc05::smem_u32(&sm.acc_full[buf]), uint32_t(use & 1), kWaitLimitNs);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) set_abort(sm, a.err);
+        break;
+      }
+      if (__shfl_sync(0xffffffffu, aborted(sm) ? 1 : 0, 0)) break;
+      tc05::fence_after_sync();
+      const Tile t = tile_of(a, idx);
+      const int row0 = t.m0 + 32 * quarter;  // position of this warp's first row
+      const int pos = row0 + lane;           // this thread's position
+      const bool valid = pos < a.n_tokens;
+      const uint32_t tbase = tmem + uint32_t(buf * kBN) + (uint32_t(32 * quarter) << 16);
+      const int64_t row_elems = a.kv_dim;
+      double* out_rows = (t.mat ? a.out[1] : a.out[0]) + (int64_t(t.layer) * a.n_tokens + row0) * row_elems + t.c0;
+      double* out_mine = out_rows + int64_t(lane) * row_elems;
+      const KvtLayer& L = a.layers[t.layer];
+      const float* ch = t.mat ? L.ch[1] : L.ch[0];
+      const float* bias = t.mat ? L.bias[1] : L.bias[0];
+      const double sx =
+          (a.use_rope && valid) ? double(__ldg(a.scale_x + int64_t(pos) * a.sx_t + int64_t(t.layer) * a.sx_l)) : 0.0;
+      const double scale = __dmul_rn(double(t.mat ? L.sw[1] : L.sw[0]), sx);
+      const bool rope_k = a.use_rope && t.mat == 0;
+      const int half = a.head_dim >> 1;
+
+      if (FAST) {
+        if (rope_k) {
+          // K: per head, out[i] = k[i] c - k[i+half] s, out[i+half] = k[i+half] c + k[i] s
+          // (rope.rs:48-57); 32 pairs per step, lo and hi halves staged as two chunks.
+          for (int hb = 0; hb < t.nvalid; hb += a.head_dim) {
+            for (int q = 0; q < half; q += kChunk) {
+              uint32_t lo[kChunk], hi[kChunk];
+              tc05::tmem_ld2_wait<kChunk>(tbase + hb + q, tbase + hb + half + q, lo, hi);
+              const double2* cs = a.rope + int64_t(q) * a.rope_rows + (valid ? pos : 0);
+#pragma unroll
+              for (int j = 0; j < kChunk; j += 2) {
+                double vlo[2], vhi[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int c = t.c0 + hb + q + j + u;
+                  const double kl = deq(int32_t(lo[j + u]), c, ch, sx, scale, bias);
+                  const double kh = deq(int32_t(hi[j + u]), c + half, ch, sx, scale, bias);
+                  const double2 w = __ldg(cs + int64_t(j + u) * a.rope_rows);
+                  vlo[u] = __dsub_rn(__dmul_rn(kl, w.x), __dmul_rn(kh, w.y));
+                  vhi[u] = __dadd_rn(__dmul_rn(kh, w.x), __dmul_rn(kl, w.y));
+                }
+                stage_pair(stage0, lane, j / 2, vlo[0], vlo[1]);
+                stage_pair(stage1, lane, j / 2, vhi[0], vhi[1]);
+              }
+              __syncwarp();
+              store_chunk(stage0, lane, out_rows, row_elems, row0, a.n_tokens, hb + q);
+              store_chunk(stage1, lane, out_rows, row_elems, row0, a.n_tokens, hb + half + q);
+              __syncwarp();
+            }
+          }
+        } else {
+          for (int cb = 0; cb < t.nvalid; cb += kChunk) {
+            uint32_t r[kChunk];
+            tc05::tmem_ld_wait<kChunk>(tbase + cb, r);
+            uint8_t* stg = (cb / kChunk) & 1 ? stage1 : stage0;
+#pragma unroll
+            for (int j = 0; j < kChunk; j += 2) {
+              double v[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+                v[u] = a.use_rope ? deq(int32_t(r[j + u]), t.c0 + cb + j + u, ch, sx, scale, bias)
+                                  : double(min(127, max(-128, int32_t(r[j + u]))));  // toy: lib.rs:307-316
+              stage_pair(stg, lane, j / 2, v[0], v[1]);
+            }
+            __syncwarp();
+            store_chunk(stg, lane, out_rows, row_elems, row0, a.n_tokens, cb);
+          }
+          __syncwarp();
         }
       } else {
-        // K: per head, out[i] = k[i] c - k[i+half] s, out[i+half] = k[i+half] c + k[i] s
-        // (rope.rs:48-57); the tile holds whole heads.
-        const int half = a.head_dim >> 1;
-        const double2* cs_row = a.rope + int64_t(valid ? t : 0) * half;
-        for (int hb = 0; hb < nvalid; hb += a.head_dim) {
-          for (int q = 0; q < half; q += G) {
-            uint32_t lo[G], hi[G];
-            tc05::tmem_ld2_wait<G>(tbase + hb + q, tbase + hb + half + q, lo, hi);
+        if (rope_k) {
+          for (int hb = 0; hb < t.nvalid; hb += a.head_dim) {
+            for (int q = 0; q < half; q += G) {
+              uint32_t lo[G], hi[G];
+              tc05::tmem_ld2_wait<G>(tbase + hb + q, tbase + hb + half + q, lo, hi);
+              if (valid) {
+                const double2* cs = a.rope + int64_t(q) * a.rope_rows + pos;
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                  const int c = t.c0 + hb + q + j;
+                  const double kl = deq(int32_t(lo[j]), c, ch, sx, scale, bias);
+                  const double kh = deq(int32_t(hi[j]), c + half, ch, sx, scale, bias);
+                  const double2 w = __ldg(cs + int64_t(j) * a.rope_rows);
+                  out_mine[hb + q + j] = __dsub_rn(__dmul_rn(kl, w.x), __dmul_rn(kh, w.y));
+                  out_mine[hb + half + q + j] = __dadd_rn(__dmul_rn(kh, w.x), __dmul_rn(kl, w.y));
+                }
+              }
+            }
+          }
+        } else {
+          for (int cb = 0; cb < t.nvalid; cb += 32) {
+            uint32_t r[32];
+            tc05::tmem_ld_wait<32>(tbase + cb, r);
             if (valid) {
 #pragma unroll
-              for (int j = 0; j < G; ++j) {
-                const int c = c0 + hb + q + j;
-                const double kl = deq(int32_t(lo[j]), c, ch, sx, scale, bias);
-                const double kh = deq(int32_t(hi[j]), c + half, ch, sx, scale, bias);
-                const double2 w = cs_row[q + j];
-                out[hb + q + j] = __dsub_rn(__dmul_rn(kl, w.x), __dmul_rn(kh, w.y));
-                out[hb + half + q + j] = __dadd_rn(__dmul_rn(kh, w.x), __dmul_rn(kl, w.y));
-              }
+              for (int j = 0; j < 32; ++j)
+                if (cb + j < t.nvalid)
+                  out_mine[cb + j] = a.use_rope ? deq(int32_t(r[j]), t.c0 + cb + j, ch, sx, scale, bias)
+                                                : double(min(127, max(-128, int32_t(r[j]))));
             }
           }
         }
       }
+      // this accumulator may now be overwritten by the MMAs of the tile after next
+      tc05::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc05::mbar_arrive(tc05::smem_u32(&sm.acc_empty[buf]));
     }
   }
 
   tc05::fence_before_sync();
   __syncthreads();
   if (warp == 0) {
+    __syncwarp();
     tc05::fence_after_sync();
-    tc05::tmem_dealloc(tmem, kBN);
+    tc05::tmem_dealloc(tmem, 2 * kBN);
   }
 }
 
-template <int G>
-cudaError_t launch_g(const KvtArgs& a, int n_layers, cudaStream_t s) {
+template <int G, bool FAST>
+cudaError_t launch_g(const KvtArgs& a, int n_sm, cudaStream_t s) {
   const size_t smem = sizeof(Smem) + 1024;
   const cudaError_t e =
-      cudaFuncSetAttribute(kv_transcript_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      cudaFuncSetAttribute(kv_transcript_kernel<G, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  const dim3 grid(2 * a.tiles_per_mat, (a.n_tokens + kBM - 1) / kBM, n_layers);
-  kv_transcript_kernel<G><<<grid, kThreads, smem, s>>>(a);
+  const int grid = std::max(1, std::min(a.n_tiles, n_sm));
+  kv_transcript_kernel<G, FAST><<<grid, kThreads, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -241,15 +380,13 @@ EncodeTiledFn encode_tiled_fn() {
 }
 
 __attribute__((noinline)) void fill_cos(double* out, const std::vector<double>& inv, int64_t n_pos) {
-  const size_t h = inv.size();
-  for (int64_t p = 0; p < n_pos; ++p)
-    for (size_t i = 0; i < h; ++i) out[2 * (p * h + i)] = std::cos(double(p) * inv[i]);
+  for (size_t i = 0; i < inv.size(); ++i)
+    for (int64_t p = 0; p < n_pos; ++p) out[2 * (int64_t(i) * n_pos + p)] = std::cos(double(p) * inv[i]);
 }
 
 __attribute__((noinline)) void fill_sin(double* out, const std::vector<double>& inv, int64_t n_pos) {
-  const size_t h = inv.size();
-  for (int64_t p = 0; p < n_pos; ++p)
-    for (size_t i = 0; i < h; ++i) out[2 * (p * h + i) + 1] = std::sin(double(p) * inv[i]);
+  for (size_t i = 0; i < inv.size(); ++i)
+    for (int64_t p = 0; p < n_pos; ++p) out[2 * (int64_t(i) * n_pos + p) + 1] = std::sin(double(p) * inv[i]);
 }
 
 }  // namespace
@@ -289,8 +426,9 @@ std::vector<double> kvt_inv_freq(int head_dim, double theta, int scaling_type, d
   return f;
 }
 
-// (cos, sin) of position * inv_freq[i] for positions [0, n_pos), interleaved
-// [n_pos][half][2], with the C library's cos and sin (rope.rs:48-52).
+// (cos, sin) of position * inv_freq[i] for positions [0, n_pos), laid out
+// [half][n_pos][2] (a warp's 32 positions are contiguous), with the C
+// library's cos and sin (rope.rs:48-52).
 void kvt_rope_table(const std::vector<double>& inv, int64_t n_pos, double* out) {
   fill_cos(out, inv, n_pos);
   fill_sin(out, inv, n_pos);
@@ -312,14 +450,15 @@ int kvt_encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t ro
   return r == CUDA_SUCCESS ? 0 : int(r);
 }
 
-cudaError_t launch_kv_transcript(const KvtArgs& a, int n_layers, cudaStream_t s) {
+cudaError_t launch_kv_transcript(const KvtArgs& a, int n_sm, cudaStream_t s) {
+  if (a.head_dim % 64 == 0) return launch_g<32, true>(a, n_sm, s);
   switch (kvt_group_width(a.head_dim)) {
-    case 1: return launch_g<1>(a, n_layers, s);
-    case 2: return launch_g<2>(a, n_layers, s);
-    case 4: return launch_g<4>(a, n_layers, s);
-    case 8: return launch_g<8>(a, n_layers, s);
-    case 16: return launch_g<16>(a, n_layers, s);
-    default: return launch_g<32>(a, n_layers, s);
+    case 1: return launch_g<1, false>(a, n_sm, s);
+    case 2: return launch_g<2, false>(a, n_sm, s);
+    case 4: return launch_g<4, false>(a, n_sm, s);
+    case 8: return launch_g<8, false>(a, n_sm, s);
+    case 16: return launch_g<16, false>(a, n_sm, s);
+    default: return launch_g<32, false>(a, n_sm, s);
   }
 }
 

@@ -120,11 +120,14 @@ struct KvtArgs {
   const KvtLayer* layers;      // [n_layers]
   const float* scale_x;        // scale_x_attn of (t, l) at t * sx_t + l * sx_l
   int64_t sx_t, sx_l;
-  const double2* rope;         // [n_tokens][head_dim / 2] (cos, sin), or nullptr (toy path)
+  const double2* rope;         // [head_dim / 2][rope_rows] (cos, sin), or nullptr (toy path)
+  int64_t rope_rows;           // positions in the table (>= n_tokens)
   double* out[2];              // K, V: [n_layers][n_tokens][kv_dim]
   int32_t n_tokens, hidden, kv_dim, head_dim;
   int32_t tile_cols;           // channels stored per tile: whole heads, <= 256
   int32_t tiles_per_mat;
+  int32_t m_tiles;             // ceil(n_tokens / 128)
+  int32_t n_tiles;             // n_layers * m_tiles * 2 * tiles_per_mat
   int32_t use_rope;
   int* err;                    // set to 2 when a bounded wait ran out
 };
@@ -135,7 +138,7 @@ std::vector<double> kvt_inv_freq(int head_dim, double theta, int scaling_type, d
 void kvt_rope_table(const std::vector<double>& inv, int64_t n_pos, double* out);
 int kvt_encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t row_stride,
                    int box_rows);
-cudaError_t launch_kv_transcript(const KvtArgs& a, int n_layers, cudaStream_t s);
+cudaError_t launch_kv_transcript(const KvtArgs& a, int n_sm, cudaStream_t s);
 
 // int_peak.cu
 cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,

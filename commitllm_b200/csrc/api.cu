@@ -768,8 +768,8 @@ vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, doubl
     return fail(VC_EINVAL, "vc_kv_transcript: x_row_stride must be >= hidden and a multiple of 16");
   if (!d->x_layers || !d->wk_layers || !d->wv_layers) return fail(VC_EINVAL, "vc_kv_transcript: NULL layer table");
   if (d->use_rope && !d->scale_x) return fail(VC_EINVAL, "vc_kv_transcript: scale_x is NULL");
-  if (reinterpret_cast<uintptr_t>(k_out) % 16 || reinterpret_cast<uintptr_t>(v_out) % 16)
-    return fail(VC_EINVAL, "vc_kv_transcript: outputs must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(k_out) % 32 || reinterpret_cast<uintptr_t>(v_out) % 32)
+    return fail(VC_EINVAL, "vc_kv_transcript: outputs must be 32-byte aligned");
   for (int l = 0; l < d->n_layers; ++l) {
     const void* p[3] = {d->x_layers[l], d->wk_layers[l], d->wv_layers[l]};
     for (const void* q : p)

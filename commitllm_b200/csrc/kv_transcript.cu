@@ -31,20 +31,18 @@ constexpr int kBM = 128;       // positions per tile (TMEM lanes)
 constexpr int kBN = 256;       // accumulator columns per tile
 constexpr int kBK = 128;       // bytes of K per stage (one swizzle row)
 constexpr int kStages = 3;
-constexpr int kEpiWarps = 4;
-constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0: TMA, warp 1: MMA, warps 2-5: epilogue
+constexpr int kEpiWarps = 8;                   // two per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0: TMA, warp 1: MMA, warps 2-9: epilogue
 constexpr uint32_t kStageA = kBM * kBK;
 constexpr uint32_t kStageB = kBN * kBK;
 constexpr uint32_t kIdesc = tc05::idesc_i8_s32(kBM, kBN);
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s per wait
 constexpr int kErrTimeout = 2;
-constexpr int kChunk = 32;                           // output columns per staged chunk
-constexpr uint32_t kStageOut = 2 * 32 * kChunk * 8;  // two [32 rows][32 cols] f64 chunks per epilogue warp
+constexpr int kStep = 16;                      // accumulator columns per TMEM load in the epilogue
 
 struct Smem {
   uint8_t a[kStages][kStageA];
   uint8_t b[kStages][kStageB];
-  uint8_t out[kEpiWarps][kStageOut];
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full[2];
@@ -93,34 +91,85 @@ __device__ __forceinline__ Tile tile_of(const KvtArgs& a, int idx) {
   return t;
 }
 
-// Staged chunk [32 rows][32 cols] f64: row r, 16-byte column pair p lives at
-// r * 256 + ((p ^ (r & 7)) * 16), so both the row-wise writes (one thread per
-// row) and the row-major reads below are free of bank conflicts.
-__device__ __forceinline__ void stage_pair(uint8_t* chunk, int r, int p, double v0, double v1) {
-  *reinterpret_cast<double2*>(chunk + r * 256 + ((p ^ (r & 7)) * 16)) = make_double2(v0, v1);
+// 32-byte store of four f64 (one full sector per lane); p 32-byte aligned.
+__device__ __forceinline__ void st_v4(double* p, const double (&v)[4]) {
+  asm volatile("st.global.v4.f64 [%0], {%1, %2, %3, %4};" ::"l"(p), "d"(v[0]), "d"(v[1]), "d"(v[2]), "d"(v[3])
+               : "memory");
 }
 
-// Warp-cooperative store of a staged chunk: 16 lanes per row, 256 contiguous
-// bytes per row, rows beyond n_tokens skipped.
-__device__ __forceinline__ void store_chunk(const uint8_t* chunk, int lane, double* out_tile, int64_t row_elems,
-                                            int row0_pos, int n_tokens, int col) {
-#pragma unroll 4
-  for (int i = 0; i < 16; ++i) {
-    const int r = 2 * i + (lane >> 4), p = lane & 15;
-    if (row0_pos + r < n_tokens) {
-      const double2 v = *reinterpret_cast<const double2*>(chunk + r * 256 + ((p ^ (r & 7)) * 16));
-      *reinterpret_cast<double2*>(out_tile + int64_t(r) * row_elems + col + 2 * p) = v;
+// Dequantisation modes, fixed per tile: toy clamp (lib.rs:307-316), per-tensor
+// scale without bias, or per-channel scales and/or bias.
+enum { kModeToy = 0, kModeTensor = 1, kModeGeneral = 2 };
+
+template <int MODE>
+__device__ __forceinline__ double dq(int32_t acc, int c, const float* ch, double sx, double scale,
+                                     const float* bias) {
+  if (MODE == kModeToy) return double(min(127, max(-128, acc)));
+  if (MODE == kModeTensor) return __dmul_rn(double(acc), scale);
+  return deq(acc, c, ch, sx, scale, bias);
+}
+
+// Epilogue of one tile for one thread (position pos) of one of the two column
+// groups: 16-column steps alternate between the groups.  Every f64 operation
+// is rounded on its own, in the reference's order.  head_dim is a multiple of
+// 64 here, so the tile holds whole heads and every step is 16 columns of one
+// half-head; results leave as 32-byte stores of four consecutive channels.
+template <int MODE>
+__device__ __forceinline__ void epilogue_fast(const KvtArgs& a, const Tile& t, uint32_t tbase, int group, int pos,
+                                              bool valid, double* out, const float* ch, const float* bias, double sx,
+                                              double scale) {
+  const int half = a.head_dim >> 1;
+  if (MODE != kModeToy && t.mat == 0) {
+    // K: per head, out[i] = k[i] c - k[i+half] s, out[i+half] = k[i+half] c + k[i] s (rope.rs:48-57)
+    int step = 0;
+    for (int hb = 0; hb < t.nvalid; hb += a.head_dim) {
+      for (int q = 0; q < half; q += kStep, ++step) {
+        if ((step & 1) != group) continue;
+        uint32_t lo[kStep], hi[kStep];
+        tc05::tmem_ld2_wait<kStep>(tbase + hb + q, tbase + hb + half + q, lo, hi);
+        if (valid) {
+          const double2* cs = a.rope + int64_t(q) * a.rope_rows + pos;
+#pragma unroll
+          for (int j = 0; j < kStep; j += 4) {
+            double olo[4], ohi[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int c = t.c0 + hb + q + j + u;
+              const double kl = dq<MODE>(int32_t(lo[j + u]), c, ch, sx, scale, bias);
+              const double kh = dq<MODE>(int32_t(hi[j + u]), c + half, ch, sx, scale, bias);
+              const double2 w = __ldg(cs + int64_t(j + u) * a.rope_rows);
+              olo[u] = __dsub_rn(__dmul_rn(kl, w.x), __dmul_rn(kh, w.y));
+              ohi[u] = __dadd_rn(__dmul_rn(kh, w.x), __dmul_rn(kl, w.y));
+            }
+            st_v4(out + hb + q + j, olo);
+            st_v4(out + hb + half + q + j, ohi);
+          }
+        }
+      }
+    }
+  } else {
+    for (int cb = kStep * group; cb < t.nvalid; cb += 2 * kStep) {
+      uint32_t r[kStep];
+      tc05::tmem_ld_wait<kStep>(tbase + cb, r);
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < kStep; j += 4) {
+          double o[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) o[u] = dq<MODE>(int32_t(r[j + u]), t.c0 + cb + j + u, ch, sx, scale, bias);
+          st_v4(out + cb + j, o);
+        }
+      }
     }
   }
 }
 
 // One persistent CTA per SM walks the tiles (layer, 128 positions, 256 channels
 // of K or V).  Warp 0 streams A/B stages with TMA, warp 1 issues the MMAs into
-// one of two TMEM accumulators, warps 2-5 turn the other accumulator into f64
+// one of two TMEM accumulators, warps 2-9 turn the other accumulator into f64
 // rows, so the epilogue of one tile overlaps the MMAs of the next.
-// FAST: head_dim a multiple of 64 (output chunks of 32 columns, staged in
-// shared memory and stored row-contiguous); otherwise one thread stores its
-// own row, RoPE pairs in groups of G columns.
+// FAST: head_dim a multiple of 64 (epilogue_fast); otherwise RoPE pairs are
+// read in groups of G columns and stored one f64 at a time.
 template <int G, bool FAST>
 __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -221,8 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArg
     // --------------------------------------------------------------- epilogue
     const int e = warp - 2;
     const int quarter = warp & 3;  // this warp may read TMEM lanes 32 * quarter .. + 31
-    uint8_t* stage0 = sm.out[e];
-    uint8_t* stage1 = sm.out[e] + kStageOut / 2;
+    const int group = e >> 2;      // which column steps of the tile (two warps per quarter)
     int it = 0;
     for (int idx = blockIdx.x; idx < a.n_tiles; idx += gridDim.x, ++it) {
       const int buf = it & 1, use = it >> 1;
@@ -236,13 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArg
       if (__shfl_sync(0xffffffffu, aborted(sm) ? 1 : 0, 0)) break;
       tc05::fence_after_sync();
       const Tile t = tile_of(a, idx);
-      const int row0 = t.m0 + 32 * quarter;  // position of this warp's first row
-      const int pos = row0 + lane;           // this thread's position
+      const int pos = t.m0 + 32 * quarter + lane;  // this thread's position
       const bool valid = pos < a.n_tokens;
       const uint32_t tbase = tmem + uint32_t(buf * kBN) + (uint32_t(32 * quarter) << 16);
-      const int64_t row_elems = a.kv_dim;
-      double* out_rows = (t.mat ? a.out[1] : a.out[0]) + (int64_t(t.layer) * a.n_tokens + row0) * row_elems + t.c0;
-      double* out_mine = out_rows + int64_t(lane) * row_elems;
+      double* out_mine = (t.mat ? a.out[1] : a.out[0]) + (int64_t(t.layer) * a.n_tokens + (valid ? pos : 0)) * a.kv_dim + t.c0;
       const KvtLayer& L = a.layers[t.layer];
       const float* ch = t.mat ? L.ch[1] : L.ch[0];
       const float* bias = t.mat ? L.bias[1] : L.bias[0];
@@ -253,58 +298,18 @@ __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArg
       const int half = a.head_dim >> 1;
 
       if (FAST) {
-        if (rope_k) {
-          // K: per head, out[i] = k[i] c - k[i+half] s, out[i+half] = k[i+half] c + k[i] s
-          // (rope.rs:48-57); 32 pairs per step, lo and hi halves staged as two chunks.
-          for (int hb = 0; hb < t.nvalid; hb += a.head_dim) {
-            for (int q = 0; q < half; q += kChunk) {
-              uint32_t lo[kChunk], hi[kChunk];
-              tc05::tmem_ld2_wait<kChunk>(tbase + hb + q, tbase + hb + half + q, lo, hi);
-              const double2* cs = a.rope + int64_t(q) * a.rope_rows + (valid ? pos : 0);
-#pragma unroll
-              for (int j = 0; j < kChunk; j += 2) {
-                double vlo[2], vhi[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const int c = t.c0 + hb + q + j + u;
-                  const double kl = deq(int32_t(lo[j + u]), c, ch, sx, scale, bias);
-                  const double kh = deq(int32_t(hi[j + u]), c + half, ch, sx, scale, bias);
-                  const double2 w = __ldg(cs + int64_t(j + u) * a.rope_rows);
-                  vlo[u] = __dsub_rn(__dmul_rn(kl, w.x), __dmul_rn(kh, w.y));
-                  vhi[u] = __dadd_rn(__dmul_rn(kh, w.x), __dmul_rn(kl, w.y));
-                }
-                stage_pair(stage0, lane, j / 2, vlo[0], vlo[1]);
-                stage_pair(stage1, lane, j / 2, vhi[0], vhi[1]);
-              }
-              __syncwarp();
-              store_chunk(stage0, lane, out_rows, row_elems, row0, a.n_tokens, hb + q);
-              store_chunk(stage1, lane, out_rows, row_elems, row0, a.n_tokens, hb + half + q);
-              __syncwarp();
-            }
-          }
-        } else {
-          for (int cb = 0; cb < t.nvalid; cb += kChunk) {
-            uint32_t r[kChunk];
-            tc05::tmem_ld_wait<kChunk>(tbase + cb, r);
-            uint8_t* stg = (cb / kChunk) & 1 ? stage1 : stage0;
-#pragma unroll
-            for (int j = 0; j < kChunk; j += 2) {
-              double v[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-                v[u] = a.use_rope ? deq(int32_t(r[j + u]), t.c0 + cb + j + u, ch, sx, scale, bias)
-                                  : double(min(127, max(-128, int32_t(r[j + u]))));  // toy: lib.rs:307-316
-              stage_pair(stg, lane, j / 2, v[0], v[1]);
-            }
-            __syncwarp();
-            store_chunk(stg, lane, out_rows, row_elems, row0, a.n_tokens, cb);
-          }
-          __syncwarp();
-        }
+        if (!a.use_rope)
+          epilogue_fast<kModeToy>(a, t, tbase, group, pos, valid, out_mine, ch, bias, sx, scale);
+        else if (!ch && !bias)
+          epilogue_fast<kModeTensor>(a, t, tbase, group, pos, valid, out_mine, ch, bias, sx, scale);
+        else
+          epilogue_fast<kModeGeneral>(a, t, tbase, group, pos, valid, out_mine, ch, bias, sx, scale);
       } else {
         if (rope_k) {
+          int step = 0;
           for (int hb = 0; hb < t.nvalid; hb += a.head_dim) {
-            for (int q = 0; q < half; q += G) {
+            for (int q = 0; q < half; q += G, ++step) {
+              if ((step & 1) != group) continue;
               uint32_t lo[G], hi[G];
               tc05::tmem_ld2_wait<G>(tbase + hb + q, tbase + hb + half + q, lo, hi);
               if (valid) {
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) kv_transcript_kernel(const KvtArg
             }
           }
         } else {
-          for (int cb = 0; cb < t.nvalid; cb += 32) {
+          for (int cb = 32 * group; cb < t.nvalid; cb += 64) {
             uint32_t r[32];
             tc05::tmem_ld_wait<32>(tbase + cb, r);
             if (valid) {

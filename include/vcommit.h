@@ -340,7 +340,7 @@ typedef struct vc_kvt_desc {
  * a per-channel table, else acc * (sw * sx) (rope.rs:107-112); + bias; K rotated
  * per head with scaled_inv_freq (constants.rs:253-297) and the C library's
  * cos/sin (rope.rs:38-60, 88-100).  Every f64 operation is rounded on its own.
- * k_out_dev / v_out_dev: DEVICE f64 [n_layers][n_tokens][kv_dim] (16-byte
+ * k_out_dev / v_out_dev: DEVICE f64 [n_layers][n_tokens][kv_dim] (32-byte
  * aligned): KvEntry.k_roped / v_deq of (layer, position), ready for
  * vc_kv_commit with VC_DTYPE_F64 and stride_row = kv_dim.
  * Weights and x_attn base pointers must be 16-byte aligned (VC_EINVAL).

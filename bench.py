@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Trace-commitment throughput on B200 (trace bytes committed GB/s, + kv_roots/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c2t|c3|c4|c5] [--impl ours|reference]
 
 A step is one pass of the commitment hot path over one batch of synthetic
 input already resident in HBM.
@@ -47,6 +47,9 @@ WORKLOADS = {
                seq_len=512, vocab=128256, x_attn=True, steps=8),
     "c5": dict(kind="kv", name="llama3.1-70b-kv-shard", n_layers=80, n_heads=8, head_dim=128, n_seqs=4,
                seq_len=32768, paged=False, steps=8),
+    # the reference's weight-provider path: KV recomputed from x_attn (compute_kv_transcript), then committed
+    "c2t": dict(kind="kvt", name="llama3.1-8b-kv-transcript", n_layers=32, n_heads=8, head_dim=128, hidden=4096,
+                n_seqs=1, seq_len=4096, rope="llama3", steps=250),
 }
 
 
@@ -61,7 +64,15 @@ def tree_blocks(n_leaves: int) -> int:
 
 
 def algorithmic(w):
-    """(SHA blocks of the dominant kernel, other blocks, source bytes, hashed bytes, n_roots) per rank-step."""
+    """(SHA blocks of the dominant kernel, other blocks, source bytes, hashed bytes, n_roots) per rank-step.
+
+    kvt: the source bytes are the f64 KvEntry rows the reference commits on
+    this path (16 bytes per K/V element pair)."""
+    if w["kind"] == "kvt":
+        kv = w["n_heads"] * w["head_dim"]
+        leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
+        blocks = leaves * sha_blocks(16 + 16 * kv) + w["n_seqs"] * w["n_layers"] * tree_blocks(w["seq_len"])
+        return blocks, 0, leaves * kv * 16, leaves * (16 + 16 * kv), w["n_seqs"] * w["n_layers"]
     if w["kind"] == "kv":
         kv = w["n_heads"] * w["head_dim"]
         leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
@@ -217,6 +228,88 @@ class KvStep:
             roots_host.copy_(roots.view(-1), non_blocking=True)
         trees.free()
         return roots.numel()
+
+
+# ---------------------------------------------------------------------------
+# KV transcript workload (c2t): compute_kv_transcript + KV commit of its rows
+# ---------------------------------------------------------------------------
+
+class KvtStep:
+    """K/V recomputed from captured x_attn and the resident Wk/Wv weights on the
+    tensor cores (f64 dequant + RoPE), then the per-layer KV trees of those f64
+    rows; the exchange of roots at N > 1 as for the KV workloads."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import dist as D
+        self.C, self.D, self.torch = C, D, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        dev = f"cuda:{device}"
+        g = torch.Generator(device=dev)
+        g.manual_seed(3000 + rank)
+        L, H, T = w["n_layers"], w["hidden"], w["n_seqs"] * w["seq_len"]
+        self.kv = kv = w["n_heads"] * w["head_dim"]
+        # captures in token order [T, L, hidden] (one int8 row per token and layer)
+        self.x = torch.randint(-128, 128, (T, L, H), generator=g, device=dev, dtype=torch.int8)
+        self.sx = torch.rand(T, L, generator=g, device=dev) * 0.05 + 1e-3
+        self.wk = [torch.randint(-128, 128, (kv, H), generator=g, device=dev, dtype=torch.int8) for _ in range(L)]
+        self.wv = [torch.randint(-128, 128, (kv, H), generator=g, device=dev, dtype=torch.int8) for _ in range(L)]
+        self.sw = [(0.0021 + 1e-5 * l, 0.0017 + 1e-5 * l) for l in range(L)]
+        self.inp = self.inputs(self.x, self.sx)
+        self.k = ctx.empty(L, T, kv, dtype=torch.float64)
+        self.v = ctx.empty(L, T, kv, dtype=torch.float64)
+        self.view = C.kv_transcript_view(self.k, self.v)
+        self.view.seq_lens = [w["seq_len"]] * w["n_seqs"]
+        self.n_trees = w["n_seqs"] * L
+        self.plan = [D.Shard(r, r + 1, 0, self.n_trees) for r in range(world)] if world > 1 else None
+        self.roots = ctx.empty(w["n_seqs"], L, 32)
+        self.ror = ctx.empty(1, 32)
+        self.kernel_events = []     # the KV commit (dominant kernel)
+        self.kvt_events = []        # the transcript kernel
+        self.launches = 2 + (1 if world > 1 else 0)
+
+    def inputs(self, x, sx):
+        C, w = self.C, self.w
+        return C.KvTranscriptInputs(x_attn=[x[:, l] for l in range(w["n_layers"])], wk=self.wk, wv=self.wv,
+                                    scale_x=sx, n_kv_heads=w["n_heads"], head_dim=w["head_dim"], per_tensor=self.sw,
+                                    rope=C.RopeConfig(theta=500000.0, scaling=w["rope"]))
+
+    def __call__(self, timed: bool, inp=None):
+        torch, C = self.torch, self.C
+        if timed:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(self.stream)
+        C.kv_transcript(self.ctx, self.inp if inp is None else inp, self.k, self.v)
+        if timed:
+            ev[1].record(self.stream)
+        roots, _ = C.kv_commit(self.ctx, self.view, keep_trees=False, roots_out=self.roots)
+        if timed:
+            ev[2].record(self.stream)
+            self.kvt_events.append((ev[0], ev[1]))
+            self.kernel_events.append((ev[1], ev[2]))
+        if self.world > 1:
+            with torch.cuda.stream(self.stream):
+                full = self.D.gather_roots(roots.view(-1, 32), self.plan, self.world, self.n_trees)
+                C.build_trees(self.ctx, full.view(-1, 32), [0, self.world * self.n_trees], keep_trees=False,
+                              roots_out=self.ror)
+
+    def host_inputs(self):
+        return [self.x, self.sx]
+
+    def e2e_step(self, host, dev_tensors, roots_host):
+        """Public API from host captures: x_attn and scale_x copied in, weights resident."""
+        with self.torch.cuda.stream(self.stream):
+            for d, h in zip(dev_tensors, host):
+                d.copy_(h, non_blocking=True)
+        key = tuple(t.data_ptr() for t in dev_tensors)
+        if getattr(self, "_e2e_key", None) != key:
+            self._e2e_inp = self.inputs(*dev_tensors)
+            self._e2e_key = key
+        self(False, inp=self._e2e_inp)
+        with self.torch.cuda.stream(self.stream):
+            roots_host.copy_(self.roots.view(-1), non_blocking=True)
+        return self.roots.numel()
 
 
 # ---------------------------------------------------------------------------
@@ -396,10 +489,51 @@ def cpu_trace(w, n_tokens, n_threads, reps=1, seed=9):
     return sorted(ts)[len(ts) // 2]
 
 
+def cpu_kvt(w, n_pos, n_threads, seed=11):
+    """Seconds to recompute n_pos positions x all layers of the c2t transcript on the host
+    (compute_kv_transcript restated in C, one position range per thread)."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import commit_oracle as O
+    from oracle import vco
+    L, H, nh, hd = w["n_layers"], w["hidden"], w["n_heads"], w["head_dim"]
+    kv = nh * hd
+    rng = np.random.default_rng(seed)
+    x = rng.integers(-128, 128, (n_pos, L, H), dtype=np.int8)
+    wk = [rng.integers(-128, 128, (kv, H), dtype=np.int8) for _ in range(L)]
+    wv = [rng.integers(-128, 128, (kv, H), dtype=np.int8) for _ in range(L)]
+    sx = rng.random((n_pos, L), dtype=np.float32)
+    sw = np.full((L, 2), 0.002, np.float32)
+    inv = np.array(O.scaled_inv_freq(hd, 500000.0, O.RopeScaling()))
+    parts = np.array_split(np.arange(n_pos), max(1, min(n_threads, n_pos)))
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(len(parts)) as ex:
+        list(ex.map(lambda p: vco.kv_transcript(x[p], wk, wv, sx[p], nh, hd, sw=sw, inv_freq=inv), parts))
+    return time.perf_counter() - t0
+
+
 def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
     """(GB/s, threads, sample text, seconds) of the CPU restatement on a bounded sample of w."""
     ncpu = os.cpu_count() or 1
     _, _, src_full, _, _ = algorithmic(w)
+    if w["kind"] == "kvt":
+        # transcript: the reference runs compute_kv_transcript on one thread (prover/src/lib.rs:207-329);
+        # the KV trees of its f64 rows cost what the c2 trees cost (same SHA blocks per leaf)
+        threads = 1 if reference_threads else ncpu
+        n_pos = max(1, threads)
+        per_pos = cpu_kvt(w, n_pos, threads) / n_pos
+        n_pos = int(max(n_pos, min(w["seq_len"], budget_s * 0.5 / max(per_pos, 1e-6))))
+        dt_t = cpu_kvt(w, n_pos, threads)
+        wkv = dict(w, kind="kv", paged=False)
+        kv_threads = 1 if reference_threads else max(1, min(ncpu, w["n_layers"]))
+        layers = max(1, min(w["n_layers"], kv_threads))
+        dt_h = cpu_kv(wkv, layers, kv_threads)
+        positions = w["n_seqs"] * w["seq_len"]
+        total = dt_t * positions / n_pos + dt_h * w["n_layers"] / layers
+        sample = (f"transcript of {n_pos} of {positions} positions x {w['n_layers']} layers ({dt_t:.2f} s, "
+                  f"{threads} thread(s)) + KV trees of {layers} of {w['n_layers']} layers ({dt_h:.2f} s, "
+                  f"{kv_threads} thread(s)), oracle C restatement, extrapolated linearly to the workload")
+        return src_full / total / 1e9, threads, sample, total
     if w["kind"] == "kv":
         # the reference hashes KV trees in a sequential per-layer loop (prover/src/lib.rs:454-478)
         threads = 1 if reference_threads else max(1, min(ncpu, w["n_seqs"] * w["n_layers"]))
@@ -486,7 +620,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     stream = torch.cuda.Stream(local)
     ctx = C.Context(local, stream)
-    step = (KvStep if w["kind"] == "kv" else TraceStep)(w, ctx, stream, local, rank, world)
+    step = {"kv": KvStep, "kvt": KvtStep, "trace": TraceStep}[w["kind"]](w, ctx, stream, local, rank, world)
     torch.cuda.synchronize()
     blocks, other_blocks, src_bytes, msg_bytes, n_roots = algorithmic(w)
 
@@ -497,6 +631,8 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     step.kernel_events.clear()
+    if hasattr(step, "kvt_events"):
+        step.kvt_events.clear()
 
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -523,7 +659,7 @@ def main():
     # the token-level IO chain of the KV workloads' sequences, timed on its own
     # (serial: one warp per sequence; not part of the KV step above)
     io_chain = None
-    if w["kind"] == "kv":
+    if w["kind"] in ("kv", "kvt"):
         S, T = w["n_seqs"], w["seq_len"]
         g = torch.Generator(device=f"cuda:{local}")
         g.manual_seed(77)
@@ -554,6 +690,35 @@ def main():
     peak_ops = C.int_peak(ctx, 0, 4000)
     ctx.sync(timeout_ms=600000)
 
+    # the transcript kernel against cuBLAS int8 (torch._int_mm, 8192^3) on the same GPU, same run
+    transcript = None
+    if w["kind"] == "kvt":
+        tms = [a.elapsed_time(b) for a, b in step.kvt_events]
+        t_avg = sum(tms) / len(tms)
+        T = w["n_seqs"] * w["seq_len"]
+        ops = 2.0 * T * 2 * step.kv * w["hidden"] * w["n_layers"]
+        with torch.cuda.stream(stream):
+            ga = torch.randint(-128, 128, (8192, 8192), device=f"cuda:{local}", dtype=torch.int8)
+            gb = torch.randint(-128, 128, (8192, 8192), device=f"cuda:{local}", dtype=torch.int8).t()
+            for _ in range(3):
+                torch._int_mm(ga, gb)
+            ms_l = []
+            for _ in range(10):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                torch._int_mm(ga, gb)
+                b.record(stream)
+                b.synchronize()
+                ms_l.append(a.elapsed_time(b))
+        int8_peak = 2.0 * 8192 ** 3 / (min(ms_l) * 1e-3) / 1e12
+        del ga, gb
+        out_bytes = 2.0 * T * step.kv * 8 * w["n_layers"]
+        transcript = {"kernel": "kv_transcript_kernel", "kernel_ms": round(t_avg, 4), "bound": "tensor",
+                      "achieved": round(ops / (t_avg * 1e-3) / 1e12, 1), "peak": round(int8_peak, 1),
+                      "unit": "int8 TOP/s", "frac": round(ops / (t_avg * 1e-3) / 1e12 / int8_peak, 4),
+                      "peak_source": "cuBLAS int8 GEMM (torch._int_mm, 8192^3, best of 10), this GPU, this run",
+                      "f64_written_GBps": round(out_bytes / (t_avg * 1e-3) / 1e9, 1)}
+
     # end to end through the public API from pinned host memory
     e2e = None
     if not args.no_e2e:
@@ -582,12 +747,12 @@ def main():
             with torch.cuda.stream(stream):
                 return estep.e2e_step(host, dev, roots_host)
 
-        for _ in range(3 if w["kind"] == "kv" else 1):
+        for _ in range(3 if w["kind"] != "trace" else 1):
             e2e_step()
         torch.cuda.synchronize()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
-        n_e2e = max(3, min(args.steps, 10)) if w["kind"] == "kv" else 2
+        n_e2e = max(3, min(args.steps, 10)) if w["kind"] != "trace" else 2
         d2h = 0
         a.record(stream)
         for _ in range(n_e2e):
@@ -636,7 +801,7 @@ def main():
                      "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not args.seqs else None,
                      "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC and not args.seqs else None,
                      "algorithmic_bytes": src_bytes,
-                     "kernel": "kv_commit_kernel" if w["kind"] == "kv" else "trace_leaf_kernel",
+                     "kernel": "trace_leaf_kernel" if w["kind"] == "trace" else "kv_commit_kernel",
                      "kernel_ms": round(k_avg, 4), "sha_blocks": blocks, "ops_per_block": BLK_OPS,
                      "peak_source": "vc_int_peak SHA-mix probe, this GPU, this run",
                      "hbm": {"achieved": round(hbm_achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -644,11 +809,14 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "io_chain": io_chain,
+        "transcript": transcript,
         "gpu_launches": args.steps * step.launches,
         "clocks": clk.summary(),
     }
-    if w["kind"] == "kv":
+    if w["kind"] in ("kv", "kvt"):
         line["kv_roots_per_s"] = line["roots_per_s"]
+    if w["kind"] == "kvt":
+        line["config"]["source_bytes"] = "f64 KvEntry rows committed (16 B per K/V element pair)"
     print(json.dumps(line), flush=True)
 
 

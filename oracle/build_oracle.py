@@ -23,7 +23,9 @@ def build(force: bool = False) -> str:
     os.makedirs(OUT, exist_ok=True)
     # No -march=native: the library also runs on the GPU host's CPU; OpenSSL
     # picks SHA-NI at run time.
-    cmd = ["gcc", "-O3", "-fPIC", "-shared", "-pthread", src, "-o", LIB + ".tmp", "-lcrypto"]
+    # -ffp-contract=off: every f64 product and sum rounds on its own, as in Rust.
+    cmd = ["gcc", "-O3", "-ffp-contract=off", "-fPIC", "-shared", "-pthread", src, "-o", LIB + ".tmp",
+           "-lcrypto", "-lm"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{r.stderr}")

@@ -11,6 +11,7 @@
  *   hash_retained_state_direct merkle.rs:144-161, wraps 170-241
  *   io_hash_v4 / io_genesis_v4 / hash_prompt  merkle.rs:250-257, 561-577
  *   the KV-tree loop of commit_minimal  crates/verilm-prover/src/lib.rs:449-482
+ *   compute_kv_transcript      crates/verilm-prover/src/lib.rs:207-329 (per-tensor / toy)
  * SHA-256 is OpenSSL's (FIPS 180-4, SHA-NI when the CPU has it), standing in
  * for the sha2 0.10.9 crate the reference uses (Cargo.lock:783-784), which
  * also dispatches to SHA-NI at run time.
@@ -19,6 +20,7 @@
  * per-layer loop; n_threads > 1 hashes distinct trees on distinct threads.
  */
 #define _GNU_SOURCE
+#include <math.h>
 #include <openssl/sha.h>
 #include <pthread.h>
 #include <stdint.h>
@@ -314,4 +316,55 @@ void vco_sha_probe(const uint8_t* buf, int64_t len, int64_t n, int n_threads) {
   for (int i = 0; i < n_threads; ++i) pthread_create(&th[i], NULL, sha_worker, &j);
   for (int i = 0; i < n_threads; ++i) pthread_join(th[i], NULL);
   free(th);
+}
+
+/* compute_kv_transcript (crates/verilm-prover/src/lib.rs:207-329), per-tensor
+ * scales or the toy path, on one thread as the reference runs it.  For each
+ * position t and layer l: k_acc / v_acc = matmul_i32 (matmul.rs:12-22, one i32
+ * dot product per output row), then acc * (sw * sx) (rope.rs:107-112) and, for
+ * K, RoPE per head with the C library's cos/sin (rope.rs:38-60); toy path
+ * (sw == NULL): clamp to i8 (verilm-core/src/lib.rs:22-24).
+ * x: [n_tok][n_layers][hidden]; wk[l], wv[l]: [kv][hidden]; scale_x:
+ * [n_tok][n_layers]; sw: [n_layers][2] (K, V) or NULL; inv_freq: [head_dim/2].
+ * Outputs [n_layers][n_tok][kv]. */
+void vco_kv_transcript(int32_t n_tok, int32_t n_layers, int32_t hidden, int32_t n_heads, int32_t head_dim,
+                       const int8_t* x, const int8_t* const* wk, const int8_t* const* wv, const float* scale_x,
+                       const float* sw, const double* inv_freq, double* k_out, double* v_out) {
+    const int64_t kv = (int64_t)n_heads * head_dim;
+    const int half = head_dim / 2;
+    double* kf = (double*)malloc(sizeof(double) * kv);
+    for (int32_t t = 0; t < n_tok; ++t) {
+        for (int32_t l = 0; l < n_layers; ++l) {
+            const int8_t* xr = x + ((int64_t)t * n_layers + l) * hidden;
+            double* ko = k_out + ((int64_t)l * n_tok + t) * kv;
+            double* vo = v_out + ((int64_t)l * n_tok + t) * kv;
+            for (int m = 0; m < 2; ++m) {
+                const int8_t* w = m ? wv[l] : wk[l];
+                double* dst = m ? vo : kf;
+                const double scale = sw ? (double)sw[2 * l + m] * (double)scale_x[(int64_t)t * n_layers + l] : 0.0;
+                for (int64_t r = 0; r < kv; ++r) {
+                    const int8_t* wr = w + r * hidden;
+                    int32_t acc = 0;
+                    for (int32_t c = 0; c < hidden; ++c) acc += (int32_t)wr[c] * (int32_t)xr[c];
+                    if (!sw) dst[r] = (double)(acc < -128 ? -128 : acc > 127 ? 127 : acc);
+                    else dst[r] = (double)acc * scale;
+                }
+            }
+            if (!sw) {
+                memcpy(ko, kf, sizeof(double) * kv);
+                continue;
+            }
+            for (int h = 0; h < n_heads; ++h) {
+                const double* hv = kf + (int64_t)h * head_dim;
+                double* o = ko + (int64_t)h * head_dim;
+                for (int i = 0; i < half; ++i) {
+                    const double a = (double)t * inv_freq[i];
+                    const double c = cos(a), s = sin(a);
+                    o[i] = hv[i] * c - hv[i + half] * s;
+                    o[i + half] = hv[i + half] * c + hv[i] * s;
+                }
+            }
+        }
+    }
+    free(kf);
 }

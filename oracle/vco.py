@@ -37,6 +37,8 @@ def lib():
         l.vco_io_chain.argtypes = [P, P, ctypes.c_int64, P, ctypes.c_int64, P]
         l.vco_sha_probe.restype = None
         l.vco_sha_probe.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int]
+        l.vco_kv_transcript.restype = None
+        l.vco_kv_transcript.argtypes = [ctypes.c_int32] * 5 + [P] * 8
         _lib = l
     return _lib
 
@@ -69,3 +71,24 @@ def io_chain(leaves: np.ndarray, token_ids, prompt: bytes) -> np.ndarray:
     out = np.zeros_like(leaves)
     lib().vco_io_chain(_ptr(leaves), _ptr(tok), leaves.shape[0], _ptr(pr), len(prompt), _ptr(out))
     return out
+
+
+def kv_transcript(x: np.ndarray, wk, wv, scale_x: np.ndarray, n_heads: int, head_dim: int, sw=None,
+                  inv_freq=None):
+    """compute_kv_transcript in C, one thread (per-tensor scales ``sw`` [n_layers][2] or the toy path).
+    x: int8 [n_tok][n_layers][hidden]; returns (k, v) f64 [n_layers][n_tok][kv]."""
+    x = np.ascontiguousarray(x, np.int8)
+    n_tok, n_layers, hidden = x.shape
+    kv = n_heads * head_dim
+    wk = [np.ascontiguousarray(w, np.int8) for w in wk]
+    wv = [np.ascontiguousarray(w, np.int8) for w in wv]
+    pk = (ctypes.c_void_p * n_layers)(*[w.ctypes.data for w in wk])
+    pv = (ctypes.c_void_p * n_layers)(*[w.ctypes.data for w in wv])
+    sx = np.ascontiguousarray(scale_x, np.float32)
+    swa = None if sw is None else np.ascontiguousarray(sw, np.float32)
+    inv = np.ascontiguousarray(inv_freq if inv_freq is not None else np.zeros(max(1, head_dim // 2)), np.float64)
+    k = np.empty((n_layers, n_tok, kv), np.float64)
+    v = np.empty((n_layers, n_tok, kv), np.float64)
+    lib().vco_kv_transcript(n_tok, n_layers, hidden, n_heads, head_dim, _ptr(x), pk, pv, _ptr(sx),
+                            None if swa is None else _ptr(swa), _ptr(inv), _ptr(k), _ptr(v))
+    return k, v

@@ -593,11 +593,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seqs", type=int, default=None, help="override the workload's sequence count")
+    ap.add_argument("--layers", type=int, default=None, help="override the workload's layer count (small captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = dict(WORKLOADS[args.workload])
     if args.seqs:
         w["n_seqs"] = args.seqs
+    if args.layers:
+        w["n_layers"] = args.layers
     if args.steps is None:
         # about a second of timed work, so the clock sampler sees the region
         args.steps = w["steps"] if args.impl == "ours" else 5
@@ -798,8 +801,8 @@ def main():
         "hashed_msg_GBps": round(msg_bytes * world / (ms_step * 1e-3) / 1e9, 3),
         "roofline": {"bound": "int_alu", "achieved": round(alu_achieved, 3), "peak": round(alu_peak, 3),
                      "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4),
-                     "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not args.seqs else None,
-                     "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC and not args.seqs else None,
+                     "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not (args.seqs or args.layers) else None,
+                     "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC and not (args.seqs or args.layers) else None,
                      "algorithmic_bytes": src_bytes,
                      "kernel": "trace_leaf_kernel" if w["kind"] == "trace" else "kv_commit_kernel",
                      "kernel_ms": round(k_avg, 4), "sha_blocks": blocks, "ops_per_block": BLK_OPS,

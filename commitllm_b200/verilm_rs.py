@@ -10,14 +10,17 @@ Same entry points, argument meanings and errors as
 
 The hashing runs on the GPU through libvcommit; inputs may be host buffers
 (copied once to the device) or CUDA tensors (read in place).  KV roots come
-from the device KV cache (``kv_cache=``), committing the same leaf encoding
-``hash_kv_entry`` (merkle.rs:285-293) over the cache's values widened to f64.
+either, as in the reference, from ``compute_kv_transcript`` when both
+``x_attn_inputs`` and a ``weight_provider`` are given (verilm-py/src/lib.rs:
+941-955; recomputed on the tensor cores from weights already on the GPU, see
+:class:`WeightProvider`), or from the device KV cache (``kv_cache=``),
+committing the same leaf encoding ``hash_kv_entry`` (merkle.rs:285-293) over
+the cache's values widened to f64.
 
 Not provided here (outside the commitment hot path): the deployment-manifest
-hash (``manifest=`` raises NotImplementedError), ``compute_kv_transcript``
-from captured x_attn and weights (``weight_provider=`` is accepted for
-signature compatibility but unused), and ``audit_v4``'s shell opening.
-Openings of the committed trees are available as ``*_proof`` methods.
+hash (``manifest=`` raises NotImplementedError), loading weights from a
+safetensors directory, and ``audit_v4``'s shell opening.  Openings of the
+committed trees are available as ``*_proof`` methods.
 """
 from __future__ import annotations
 
@@ -29,6 +32,139 @@ import numpy as np
 import torch
 
 from . import commit as C
+
+# MatrixType::PER_LAYER order (crates/verilm-core/src/constants.rs:26-34)
+MATRIX_TYPES = ("Wq", "Wk", "Wv", "Wo", "Wg", "Wu", "Wd")
+
+
+class ModelConfig:
+    """The fields of ``ModelConfig`` (constants.rs:139-157) that
+    ``compute_kv_transcript`` reads.  ``rope_scaling``: None or a dict with
+    ``rope_type``, ``factor``, ``low_freq_factor``, ``high_freq_factor``,
+    ``original_max_position_embeddings`` (constants.rs:126-137)."""
+
+    def __init__(self, n_layers: int, hidden_dim: int, n_kv_heads: int, d_head: int, rope_theta: float,
+                 rope_scaling: Optional[dict] = None):
+        self.n_layers, self.hidden_dim = int(n_layers), int(hidden_dim)
+        self.n_kv_heads, self.d_head = int(n_kv_heads), int(d_head)
+        self.kv_dim = self.n_kv_heads * self.d_head
+        self.rope_theta = float(rope_theta)
+        self.rope_scaling = rope_scaling
+
+
+class WeightProvider:
+    """The K/V-projection part of the reference's ``WeightProvider``
+    (verilm-py/src/lib.rs:530-555; accessors verilm-keygen/src/lib.rs:1202-1232),
+    built from tensors a serving engine already holds on the GPU instead of
+    loaded from a safetensors directory.
+
+    wk, wv: per layer int8 CUDA tensors ``[kv_dim, hidden]``; weight_scales:
+    per layer 7 per-tensor scales in ``MATRIX_TYPES`` order (0.0 for native
+    INT8), or empty; per_channel_weight_scales: per layer 7 entries (float32
+    ``[out_dim]`` tensors or None; only Wk and Wv are read), or empty;
+    qkv_biases: per layer ``[q_bias, k_bias, v_bias]`` (float32 or None), or
+    empty.  Empty lists mean what they mean in the reference: no per-tensor /
+    per-channel scales (both empty: the toy path), no biases.
+    """
+
+    def __init__(self, config: ModelConfig, wk, wv, weight_scales=(), per_channel_weight_scales=(),
+                 qkv_biases=()):
+        self._config = config
+        self._w = {"Wk": list(wk), "Wv": list(wv)}
+        self._scales = [list(s) for s in weight_scales]
+        self._pc = [list(s) for s in per_channel_weight_scales]
+        self._bias = [list(b) for b in qkv_biases]
+        if len(self._w["Wk"]) < config.n_layers or len(self._w["Wv"]) < config.n_layers:
+            raise ValueError("wk and wv need one tensor per layer")
+
+    def config(self) -> ModelConfig:
+        return self._config
+
+    def weight(self, layer: int, mt: str) -> torch.Tensor:
+        if mt not in self._w:
+            raise ValueError(f"only Wk and Wv are held here, not {mt}")
+        return self._w[mt][layer]
+
+    def weight_scales(self):
+        return self._scales
+
+    def per_channel_weight_scales(self):
+        return self._pc
+
+    def qkv_biases(self):
+        return self._bias
+
+
+def _kv_transcript_from_captures(ctx: C.Context, wp: WeightProvider, x_attn_inputs, scales_d: torch.Tensor,
+                                 fwd_batch_sizes, n_layers: int):
+    """``build_retained_from_captures``' x_attn (prover/src/lib.rs:139-181) and
+    ``compute_kv_transcript`` (prover/src/lib.rs:207-329) on the GPU: the
+    captured rows are gathered into ``[n_tokens, layers, hidden]`` on the
+    device, scale_x_attn is the qkv block of each entry's scales
+    (verilm-py/src/lib.rs:859-866).  Returns f64 ``k, v`` ``[layers, n_tokens, kv_dim]``."""
+    cfg = wp.config()
+    n_entries = len(fwd_batch_sizes) * n_layers
+    if len(x_attn_inputs) < n_entries:
+        raise ValueError("x_attn_inputs must hold one entry per (forward pass, layer)")
+    L = min(cfg.n_layers, n_layers)
+    n_tok = sum(fwd_batch_sizes)
+    H = cfg.hidden_dim
+    dev = f"cuda:{ctx.device}"
+    with torch.cuda.stream(ctx.stream):
+        X = torch.empty(n_tok, L, H, dtype=torch.int8, device=dev)
+        sx_idx = torch.empty(n_tok, L, dtype=torch.long)
+        t0 = cursor = e = 0
+        for bs in fwd_batch_sizes:
+            for l in range(n_layers):
+                xa = x_attn_inputs[e]
+                if isinstance(xa, torch.Tensor) and xa.is_cuda:
+                    src = xa.reshape(-1).view(torch.int8)
+                else:
+                    src = ctx.to_device(_u8_host(xa)).view(torch.int8)
+                if src.numel() != bs * H:
+                    raise ValueError(f"x_attn entry {e} holds {src.numel()} bytes, expected {bs} x {H}")
+                if l < L:
+                    X[t0:t0 + bs, l].copy_(src.view(bs, H))
+                    sx_idx[t0:t0 + bs, l] = torch.arange(cursor, cursor + bs)     # the qkv block
+                cursor += 4 * bs
+                e += 1
+            t0 += bs
+        sx = scales_d.index_select(0, sx_idx.view(-1).to(dev)).view(n_tok, L)
+
+    def pair(seq, l, conv):
+        if not seq or l >= len(seq) or seq[l] is None:
+            return None
+        row = seq[l]
+        k, v = (row[1], row[2]) if len(row) > 2 else (None, None)
+        return (conv(k), conv(v))
+
+    def dev_f32(t):
+        if t is None:
+            return None
+        if isinstance(t, torch.Tensor) and t.numel() == 0:
+            return None
+        if not isinstance(t, torch.Tensor) and len(t) == 0:
+            return None
+        return ctx.to_device(t if isinstance(t, torch.Tensor) else np.asarray(t, np.float32), dtype=torch.float32)
+
+    ws, pc, qb = wp.weight_scales(), wp.per_channel_weight_scales(), wp.qkv_biases()
+    per_tensor = [(float(ws[l][1]) if len(ws[l]) > 1 else 0.0, float(ws[l][2]) if len(ws[l]) > 2 else 0.0)
+                  for l in range(min(L, len(ws)))] if ws else None
+    per_channel = [pair(pc, l, dev_f32) for l in range(L)] if pc else None
+    biases = [pair(qb, l, dev_f32) for l in range(L)] if qb else None
+    rs = cfg.rope_scaling
+    rope = C.RopeConfig(theta=cfg.rope_theta)
+    if rs:
+        rope = C.RopeConfig(theta=cfg.rope_theta, scaling=rs.get("rope_type"), factor=rs.get("factor", 8.0),
+                            low_freq_factor=rs.get("low_freq_factor", 1.0),
+                            high_freq_factor=rs.get("high_freq_factor", 4.0),
+                            original_max_position_embeddings=rs.get("original_max_position_embeddings", 8192))
+    inp = C.KvTranscriptInputs(x_attn=[X[:, l] for l in range(L)], wk=[wp.weight(l, "Wk") for l in range(L)],
+                               wv=[wp.weight(l, "Wv") for l in range(L)], scale_x=sx, n_kv_heads=cfg.n_kv_heads,
+                               head_dim=cfg.d_head, per_tensor=per_tensor if per_tensor else None,
+                               per_channel=per_channel, biases=biases, rope=rope)
+    k, v = C.kv_transcript(ctx, inp)
+    return k, v, [X, sx]
 
 
 def _f32_host(x) -> np.ndarray:
@@ -334,6 +470,14 @@ def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_size
         if t is not None:
             lay.logits, lay.tok_logits_row = t, _wrap_rows(n_tok, rows, n_prompt_tokens, "logits")
             keep.append(t)
+    if x_attn_inputs is not None and weight_provider is not None:
+        # the reference's path: K/V recomputed from x_attn + weights, then committed
+        if kv_cache is not None:
+            raise ValueError("pass either kv_cache or x_attn_inputs with weight_provider, not both")
+        k, v, held = _kv_transcript_from_captures(ctx, weight_provider, x_attn_inputs, scales_d, fwd_batch_sizes,
+                                                  n_layers)
+        kv_cache = C.kv_transcript_view(k, v)
+        keep += [k, v] + held
     h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle,
                 x_attn=x_attn_inputs)
     h._inputs = keep

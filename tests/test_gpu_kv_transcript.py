@@ -159,3 +159,68 @@ def test_transcript_zero_tokens_and_errors(ctx):
     with pytest.raises(VcValueError):
         C.kv_transcript(ctx, inp)
     ctx.sync(10000)
+
+
+@pytest.mark.parametrize("mode", ["per_tensor", "per_channel_bias"])
+def test_verilm_rs_weight_provider_path(ctx, mode):
+    """commit_minimal_from_captures with x_attn_inputs + weight_provider commits the
+    recomputed transcript (verilm-py/src/lib.rs:941-970): kv_roots and KV openings
+    equal the oracle's compute_kv_transcript + hash_kv_entry trees."""
+    from commitllm_b200 import verilm_rs as V
+    rng = np.random.default_rng(31)
+    L, H, nh, hd = 3, 64, 2, 64
+    kv = nh * hd
+    fwd = [5, 1, 1, 1]
+    n = sum(fwd)
+    a = rng.integers(-128, 128, (n, L, H), dtype=np.int8)
+    x = rng.integers(-128, 128, (n, L, H), dtype=np.int8)
+    sq = (rng.random((n, L), dtype=np.float32) * 0.05 + 1e-3).astype(np.float32)   # qkv block = scale_x_attn
+    so = (rng.random((n, L), dtype=np.float32) * 0.05 + 1e-3).astype(np.float32)   # o_proj block = scale_a
+    a_list, x_list, scales = [], [], []
+    t0 = 0
+    for bs in fwd:
+        for l in range(L):
+            a_list.append(np.ascontiguousarray(a[t0:t0 + bs, l]).reshape(-1))
+            x_list.append(ctx.to_device(np.ascontiguousarray(x[t0:t0 + bs, l]).reshape(-1)))
+            scales += list(sq[t0:t0 + bs, l]) + list(so[t0:t0 + bs, l]) + [0.5] * bs + [0.25] * bs
+        t0 += bs
+    wk = [rng.integers(-128, 128, (kv, H), dtype=np.int8) for _ in range(L)]
+    wv = [rng.integers(-128, 128, (kv, H), dtype=np.int8) for _ in range(L)]
+    scal = dict(rope_type="llama3", factor=8.0, low_freq_factor=1.0, high_freq_factor=4.0,
+                original_max_position_embeddings=8192)
+    cfg = V.ModelConfig(L, H, nh, hd, 500000.0, scal)
+    if mode == "per_tensor":
+        ws = [[0.01, 0.002 * (l + 1), 0.003, 0.01, 0.01, 0.01, 0.01] for l in range(L)]
+        wp = V.WeightProvider(cfg, [ctx.to_device(w) for w in wk], [ctx.to_device(w) for w in wv], weight_scales=ws)
+        ref_kw = dict(per_tensor=[(np.float32(s[1]), np.float32(s[2])) for s in ws])
+    else:
+        pc = [[None, (rng.random(kv, dtype=np.float32) * 0.01).astype(np.float32),
+               (rng.random(kv, dtype=np.float32) * 0.01).astype(np.float32), None, None, None, None]
+              for _ in range(L)]
+        qb = [[None, rng.standard_normal(kv).astype(np.float32), rng.standard_normal(kv).astype(np.float32)]
+              for _ in range(L)]
+        wp = V.WeightProvider(cfg, [ctx.to_device(w) for w in wk], [ctx.to_device(w) for w in wv],
+                              per_channel_weight_scales=[[None if c is None else ctx.to_device(c) for c in row]
+                                                         for row in pc],
+                              qkv_biases=qb)
+        ref_kw = dict(per_channel=[(row[1], row[2]) for row in pc], biases=[(row[1], row[2]) for row in qb])
+    toks = [int(t) for t in rng.integers(0, 128256, n)]
+    h = V.commit_minimal_from_captures(a_list, np.array(scales, np.float32), L, fwd, toks, b"kv prompt", b"\x07" * 32,
+                                       weight_provider=wp, x_attn_inputs=x_list, ctx=ctx)
+    k_ref, v_ref = O.compute_kv_transcript(x, wk, wv, sq, nh, hd, rope_theta=500000.0,
+                                           rope_scaling=O.RopeScaling(), **ref_kw)
+    assert h.kv_roots_hex() == [O.kv_tree_for_layer(l, k_ref[l], v_ref[l]).root.hex() for l in range(L)]
+    # the trace leaves do not contain x_attn (prover/src/lib.rs:162-167)
+    retained = [[O.RetainedLayerState(a[t, l].tobytes(), float(so[t, l])) for l in range(L)] for t in range(n)]
+    com = O.commit_minimal(retained, toks, b"kv prompt", b"\x07" * 32)
+    assert h.merkle_root_hex() == com.merkle_root.hex() and h.io_root_hex() == com.io_root.hex()
+    # openings carry the recomputed KvEntry rows
+    layers, ent, sib = h.kv_openings(n - 1, [0, 2])
+    assert layers == [0, 2]
+    for i, l in enumerate(layers):
+        assert same_bits(ent[i, :, 0], k_ref[l]) and same_bits(ent[i, :, 1], v_ref[l])
+    with pytest.raises(ValueError):
+        V.commit_minimal_from_captures(a_list, np.array(scales, np.float32), L, fwd, toks, b"p", b"\x07" * 32,
+                                       weight_provider=wp, x_attn_inputs=x_list, ctx=ctx,
+                                       kv_cache=C.kv_transcript_view(torch.from_numpy(k_ref).cuda(),
+                                                                     torch.from_numpy(v_ref).cuda()))

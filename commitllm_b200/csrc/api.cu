@@ -639,6 +639,7 @@ vc_status vc_trace_leaves(vc_ctx* c, const vc_trace_desc* d, uint8_t* leaves_dev
   vc_status r = upload(c, st, &dev);
   if (r) return r;
   TraceArgs a{};
+  a.opq = make_opq();
   a.n_tokens = d->n_tokens;
   a.n_layers = d->n_layers;
   a.hidden = d->hidden;

@@ -10,13 +10,17 @@
 // All threads of a warp hash messages of the same layout, so the fill
 // position -- and every branch on it -- is warp-uniform.
 #pragma once
+#include "sha256_bal.cuh"
 #include "sha256_core.cuh"
 
 namespace vc {
 
-template <int NT>
+// BAL: the split of compress_bal (sha256_bal.cuh) to use, 0 for the plain
+// compression; with BAL != 0, opq must point at the opaque multipliers.
+template <int NT, int BAL = 0>
 struct Sha256Stream {
   uint32_t h[8];
+  const Opq* opq = nullptr;
   uint32_t* buf;    // this thread's column of the CTA's [16][NT] buffer
   uint32_t fill;    // bytes of the current block, pending partial word included (0..63)
   uint32_t carry;   // the fill % 4 pending bytes, left-aligned big-endian
@@ -30,11 +34,18 @@ struct Sha256Stream {
     total = 0;
   }
 
+  __device__ __forceinline__ void cmp(uint32_t w[16]) {
+    if constexpr (BAL == 0)
+      compress(h, w);
+    else
+      compress_bal<BAL>(h, w, *opq);
+  }
+
   __device__ __forceinline__ void block() {
     uint32_t w[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) w[k] = buf[k * NT];
-    compress(h, w);
+    cmp(w);
   }
 
   // Append 4 bytes given as a big-endian word.
@@ -133,7 +144,7 @@ struct Sha256Stream {
         for (int j = 0; j < 16; ++j) x[j] = __ldg(qn + j);
         x[16] = s ? __ldg(qn + 16) : 0u;
       }
-      compress(h, w);
+      cmp(w);
     }
   }
 

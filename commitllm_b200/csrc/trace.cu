@@ -6,6 +6,13 @@
 namespace vc {
 
 constexpr int kTraceThreads = 128;
+// Compression split of the retained-state leaves: the round's adds, the
+// schedule's adds and its two plain shifts go to the FMA pipe as IMADs
+// (kAddRound | kAddSched | kShrSched), the rotates and logic ops stay on the
+// ALU.  Measured on the C4 workload (256 x 512 tokens with logits): 136.0 ->
+// 125.4 ms; the KV kernel, whose messages are half zero words, keeps the
+// plain compression (the split measured slower there).
+constexpr int kTraceSplit = kAddRound | kAddSched | kShrSched;
 
 // Domain separators (ASCII), merkle.rs:147, 179, 206, 233, 251, 555, 563, 574.
 __device__ const char kTagRetained[] = "vi-retained-v3";
@@ -18,14 +25,15 @@ __device__ const char kTagGenesis[] = "vi-io-genesis-v4";
 
 // One thread per token: hash_retained_state_direct (merkle.rs:144-161), then
 // the optional wraps of hash_retained_with_captured_logits (merkle.rs:170-241).
-__global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(TraceArgs a) {
+__global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_constant__ TraceArgs a) {
   __shared__ uint32_t sbuf[16 * kTraceThreads];
   const int t = blockIdx.x * kTraceThreads + threadIdx.x;
   if (t >= a.n_tokens) return;
   const int32_t* tk = a.tok + 5 * int64_t(t);
   const int f = tk[0];
   const int64_t row = tk[1];
-  Sha256Stream<kTraceThreads> s;
+  Sha256Stream<kTraceThreads, kTraceSplit> s;
+  s.opq = &a.opq;  // parameter space (__grid_constant__): read as constant operands
   s.init(sbuf + threadIdx.x);
   s.put_tag(kTagRetained, 14);
   for (int l = 0; l < a.n_layers; ++l) {

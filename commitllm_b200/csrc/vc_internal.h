@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <vector>
 
+#include "sha256_opq.h"
+
 namespace vc {
 
 constexpr int kTreeThreads = 128;  // leaves per CTA of the Merkle kernels (chunk cap)
@@ -96,6 +98,7 @@ struct TraceArgs {
   const uint8_t* lp; int32_t lp_dim; int64_t lp_stride;
   const uint8_t* logits; int32_t vocab; int64_t logits_stride;
   uint8_t* leaves;
+  Opq opq;                      // multipliers of the balanced compression (make_opq())
 };
 cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s);
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,

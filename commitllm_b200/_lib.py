@@ -47,6 +47,7 @@ class KvDesc(ctypes.Structure):
         ("stride_page", c_int64), ("stride_row", c_int64), ("stride_head", c_int64),
         ("cache_elems", c_int64),
         ("k_layers", POINTER(c_void_p)), ("v_layers", POINTER(c_void_p)),
+        ("pos_base", POINTER(c_int64)), ("tree_log2", c_int32),
     ]
 
 

@@ -192,6 +192,10 @@ class KvCacheView:
     block_tables: Optional[torch.Tensor] = None
     seq_row_offset: Optional[Sequence[int]] = None
     layer_base: int = 0
+    # split trees (dist.split_kv_commit): leaf position of each sequence's local
+    # row 0, and a fixed subtree height (0: each tree padded to its own length)
+    pos_base: Optional[Sequence[int]] = None
+    tree_log2: int = 0
 
 
 def _kv_desc(view: KvCacheView):
@@ -250,6 +254,11 @@ def _kv_desc(view: KvCacheView):
         offs = _i64(view.seq_row_offset)
         keep.append(offs)
         d.seq_row_offset = ctypes.cast(offs, ctypes.POINTER(ctypes.c_int64))
+    if view.pos_base is not None:
+        pb = _i64(view.pos_base)
+        keep.append(pb)
+        d.pos_base = ctypes.cast(pb, ctypes.POINTER(ctypes.c_int64))
+    d.tree_log2 = int(view.tree_log2)
     kp = _ptrs([t.data_ptr() for t in view.k_layers])
     vp = _ptrs([t.data_ptr() for t in view.v_layers])
     keep += [kp, vp]
@@ -294,6 +303,7 @@ def kv_open(ctx: Context, view: KvCacheView, trees: TreeSet, seq: int, layers: S
     n_sel = len(layers)
     n = int(view.seq_lens[seq]) if 0 <= seq < len(view.seq_lens) else 1
     depth_max = max(1, (1 << (n - 1).bit_length()).bit_length() - 1) if n > 1 else 1
+    depth_max = max(depth_max, int(view.tree_log2))
     entries = ctx.empty(max(n_sel, 1), max(n_positions, 1), 2, kv, dtype=torch.float64)
     sib = ctx.empty(max(n_sel, 1), max(n_positions, 1), depth_max, 32)
     depth = ctypes.c_int32(0)

@@ -151,9 +151,11 @@ struct Plan {
   int32_t n_trees = 0;
 };
 
-void plan_group(Plan& p, int64_t n, int n_layers, int64_t src_off, int seq) {
+// lp_fixed > 0: a subtree of 2^lp_fixed leaves (split trees), n of them real.
+void plan_group(Plan& p, int64_t n, int n_layers, int64_t src_off, int seq, int64_t pos_base = 0,
+                int lp_fixed = 0) {
   TreeMeta m{};
-  const int lp = ilog2_ceil(n);
+  const int lp = lp_fixed > 0 ? lp_fixed : ilog2_ceil(n);
   const int kc = std::min(lp, kLog2TreeThreads);
   const int64_t pad = int64_t(1) << lp;
   m.n_leaves = n;
@@ -169,6 +171,7 @@ void plan_group(Plan& p, int64_t n, int n_layers, int64_t src_off, int seq) {
   m.src_off = src_off;
   m.tree_base = p.n_trees;
   m.seq = seq;
+  m.pos_base = pos_base;
   p.n_trees += n_layers;
   const int mi = int(p.meta.size());
   p.meta.push_back(m);
@@ -311,10 +314,22 @@ vc_status vc_kv_commit(vc_ctx* c, const vc_kv_desc* d, uint8_t* kv_roots_dev, vc
   if (paged && (d->block_size < 1 || d->max_blocks_per_seq < 1))
     return fail(VC_EINVAL, "vc_kv_commit: paged layout needs block_size and max_blocks_per_seq >= 1");
   const int64_t row_span = int64_t(d->n_kv_heads - 1) * d->stride_head + d->head_dim;
+  if (d->tree_log2 < 0 || d->tree_log2 > kMaxTreeHeight)
+    return fail(VC_EINVAL, "vc_kv_commit: tree_log2 %d out of range", d->tree_log2);
   int64_t acc = 0;
   for (int s = 0; s < d->n_seqs; ++s) {
     const int64_t n = d->seq_lens[s];
-    if (n < 1) return fail(VC_EINVAL, "vc_kv_commit: seq_lens[%d] = %lld (need at least one leaf)", s, (long long)n);
+    const int64_t pb = d->pos_base ? d->pos_base[s] : 0;
+    if (d->tree_log2 > 0) {
+      if (n < 0 || n > (int64_t(1) << d->tree_log2))
+        return fail(VC_EINVAL, "vc_kv_commit: seq_lens[%d] = %lld does not fit a subtree of 2^%d leaves", s,
+                    (long long)n, d->tree_log2);
+      if (n == 0) continue;
+    } else if (n < 1) {
+      return fail(VC_EINVAL, "vc_kv_commit: seq_lens[%d] = %lld (need at least one leaf)", s, (long long)n);
+    }
+    if (pb < 0 || pb + n > (int64_t(1) << 32))
+      return fail(VC_EINVAL, "vc_kv_commit: positions of seq %d do not fit the u32 position field", s);
     if (paged) {
       if ((n + d->block_size - 1) / d->block_size > d->max_blocks_per_seq)
         return fail(VC_EINVAL, "vc_kv_commit: seq %d needs more than max_blocks_per_seq pages", s);
@@ -345,10 +360,12 @@ vc_status vc_kv_commit(vc_ctx* c, const vc_kv_desc* d, uint8_t* kv_roots_dev, vc
 
   DeviceGuard g(c->device);
   Plan p;
+  std::vector<int32_t> empty;   // groups of subtrees without a real leaf
   acc = 0;
   for (int s = 0; s < d->n_seqs; ++s) {
     const int64_t r0 = d->seq_row_offset ? d->seq_row_offset[s] : acc;
-    plan_group(p, d->seq_lens[s], d->n_layers, r0, s);
+    if (d->tree_log2 > 0 && d->seq_lens[s] == 0) empty.push_back(int32_t(p.meta.size()));
+    plan_group(p, d->seq_lens[s], d->n_layers, r0, s, d->pos_base ? d->pos_base[s] : 0, d->tree_log2);
     acc += d->seq_lens[s];
   }
   if (p.items.size() > 0x7FFFFFFFull) return fail(VC_EINVAL, "vc_kv_commit: too many chunks");
@@ -356,6 +373,7 @@ vc_status vc_kv_commit(vc_ctx* c, const vc_kv_desc* d, uint8_t* kv_roots_dev, vc
   Stager st;
   const size_t o_meta = st.add(p.meta.data(), p.meta.size() * sizeof(TreeMeta));
   const size_t o_items = st.add(p.items.data(), p.items.size() * sizeof(int2));
+  const size_t o_empty = st.add(empty.data(), empty.size() * sizeof(int32_t));
   const size_t o_k = st.add(d->k_layers, sizeof(void*) * d->n_layers);
   const size_t o_v = st.add(d->v_layers, sizeof(void*) * d->n_layers);
   vc_tree_set* ts = nullptr;
@@ -394,7 +412,11 @@ vc_status vc_kv_commit(vc_ctx* c, const vc_kv_desc* d, uint8_t* kv_roots_dev, vc
       a.out.roots = kv_roots_dev;
       a.out.zero_roots = c->zero_roots;
       cudaError_t e = cudaMemsetAsync(c->scratch, 0, counters_bytes, c->stream);
-      if (e == cudaSuccess) e = launch_kv_commit(a, int(p.items.size()), d->n_layers, d->dtype, fast, c->stream);
+      if (e == cudaSuccess && !p.items.empty())
+        e = launch_kv_commit(a, int(p.items.size()), d->n_layers, d->dtype, fast, c->stream);
+      if (e == cudaSuccess)
+        e = launch_empty_trees(a.meta, reinterpret_cast<const int32_t*>(dev + o_empty), int(empty.size()),
+                               d->n_layers, a.out, c->stream);
       if (e != cudaSuccess) r = fail(VC_ECUDA, "vc_kv_commit launch: %s", cudaGetErrorString(e));
     }
   }

@@ -409,7 +409,8 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_kernel(KvArgs a) {
       rc.nh = a.n_heads;
       rc.sel = 0; rc.h = 0; rc.ci = 0;
       const int kv = a.n_heads * a.head_dim;
-      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(p), rc, kv >> 2, uint32_t(16 + 16 * kv) * 8u);
+      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(m.pos_base + p), rc, kv >> 2,
+                  uint32_t(16 + 16 * kv) * 8u);
     } else {
 #pragma unroll
       for (int w = 0; w < 8; ++w) d[w] = 0;
@@ -445,7 +446,7 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_generic_kernel(KvArgs 
       s.put_be(0x76692d6bu);
       s.put_be(0x762d7631u);
       s.put_be(bswap32(uint32_t(a.layer_base + layer)));
-      s.put_be(bswap32(uint32_t(p)));
+      s.put_be(bswap32(uint32_t(m.pos_base + p)));
       for (int sel = 0; sel < 2; ++sel) {
         const char* row = static_cast<const char*>(sel ? a.v_layers[layer] : a.k_layers[layer]) + off;
         for (int h = 0; h < a.n_heads; ++h) {
@@ -592,7 +593,8 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_noalloc_kernel(const _
       rc.nh = a.n_heads;
       rc.sel = 0; rc.h = 0; rc.ci = 0;
       const int kv = a.n_heads * a.head_dim;
-      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(p), rc, kv >> 2, uint32_t(16 + 16 * kv) * 8u);
+      kv_leaf<DT>(d, uint32_t(a.layer_base + layer), uint32_t(m.pos_base + p), rc, kv >> 2,
+                  uint32_t(16 + 16 * kv) * 8u);
     } else {
 #pragma unroll
       for (int w = 0; w < 8; ++w) d[w] = 0;
@@ -651,6 +653,8 @@ extern "C" vc_status vc_kv_commit_noalloc(const vc_kv_desc* d, uint8_t* kv_roots
                      kNoAllocMaxSeqs, kNoAllocMaxLayers, d->n_seqs, d->n_layers);
   if (d->dtype < VC_DTYPE_BF16 || d->dtype > VC_DTYPE_F64) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: bad dtype");
   if (!d->seq_lens || !d->k_layers || !d->v_layers) return set_error(VC_EINVAL, "vc_kv_commit_noalloc: NULL table");
+  if (d->pos_base || d->tree_log2 != 0)
+    return set_error(VC_ENOTSUP, "vc_kv_commit_noalloc: split trees (pos_base, tree_log2) are not supported");
   if (d->cache_elems <= 0 || d->stride_row < 0 || d->stride_head < 0 || d->stride_page < 0)
     return set_error(VC_EINVAL, "vc_kv_commit_noalloc: cache_elems must be > 0 and strides >= 0");
   const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
@@ -799,6 +803,29 @@ cudaError_t launch_kv_entries(const KvOpenArgs& a, int dtype, cudaStream_t s) {
     case 1: kv_entries_kernel<1><<<int(n), 128, 0, s>>>(a); break;
     default: kv_entries_kernel<2><<<int(n), 128, 0, s>>>(a); break;
   }
+  return cudaGetLastError();
+}
+
+// One CTA per (empty subtree, layer): every node at level k is Z_k.
+__global__ void empty_tree_kernel(const TreeMeta* meta, const int32_t* which, TreeOut o) {
+  const TreeMeta m = meta[which[blockIdx.x]];
+  const int layer = blockIdx.y;
+  const int lp = m.log2_pad;
+  if (o.nodes) {
+    uint8_t* t = o.nodes + (m.node_base + int64_t(layer) * m.node_stride) * 32;
+    for (int k = 0; k <= lp; ++k) {
+      const int64_t cnt = int64_t(1) << (lp - k);
+      uint8_t* lvl = t + level_off(lp, k) * 32;
+      for (int64_t i = threadIdx.x; i < cnt; i += blockDim.x) store_z(lvl + i * 32, o.zero_roots + 8 * k);
+    }
+  }
+  if (threadIdx.x == 0) store_z(o.roots + int64_t(m.tree_base + layer) * 32, o.zero_roots + 8 * lp);
+}
+
+cudaError_t launch_empty_trees(const TreeMeta* meta, const int32_t* which, int n_empty, int n_layers,
+                               const TreeOut& o, cudaStream_t s) {
+  if (n_empty == 0) return cudaSuccess;
+  empty_tree_kernel<<<dim3(n_empty, n_layers), kTreeThreads, 0, s>>>(meta, which, o);
   return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@ struct TreeMeta {
   int32_t tree_base;     // tree index of layer 0 (tree = tree_base + layer)
   int32_t seq;           // KV: block-table row
   int32_t pad_;
+  int64_t pos_base;      // KV: leaf position of local row 0 (split trees; 0 otherwise)
 };
 
 struct TreeOut {
@@ -81,6 +82,9 @@ cudaError_t launch_kv_entries(const KvOpenArgs& a, int dtype, cudaStream_t s);
 cudaError_t launch_kv_commit(const KvArgs& a, int n_items, int n_layers, int dtype, bool fast,
                              cudaStream_t s);
 cudaError_t launch_tree_commit(const TreeArgs& a, int n_items, cudaStream_t s);
+// Subtrees without a real leaf (split trees past the sequence's end): nodes Z_k, root Z_lp.
+cudaError_t launch_empty_trees(const TreeMeta* meta, const int32_t* which, int n_empty, int n_layers,
+                               const TreeOut& o, cudaStream_t s);
 cudaError_t launch_prove(const uint8_t* nodes, const ProveReq* reqs, int n, int max_depth,
                          uint8_t* siblings, cudaStream_t s);
 

@@ -85,3 +85,81 @@ def gather_roots(local: torch.Tensor, plan: List[Shard], n_seqs: int, n_layers: 
         got = out[r * width: r * width + sh.n_trees].view(sh.seq_end - sh.seq_begin, sh.layer_end - sh.layer_begin, 32)
         full[sh.seq_begin:sh.seq_end, sh.layer_begin:sh.layer_end].copy_(got)
     return full
+
+
+# ---------------------------------------------------------------------------
+# Split trees: one request's per-layer trees spread over the ranks by position
+# ---------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class SplitRange:
+    """Rank ``rank``'s part of a tree of ``n_leaves`` positions split over
+    ``world`` ranks: positions ``[begin, begin + count)`` (``count`` may be 0
+    past the end), inside the aligned subtree of ``2**sub_log2`` leaves that
+    starts at ``begin``; ``top_log2`` levels sit above the subtrees."""
+    rank: int
+    begin: int
+    count: int
+    sub_log2: int
+    top_log2: int
+
+
+def split_ranges(n_leaves: int, world: int) -> List[SplitRange]:
+    """Aligned power-of-two position ranges of ``n_pad / world`` leaves.
+
+    ``build_tree`` (merkle.rs:11-48) pads only level 0 with zero leaves, so the
+    tree over ``n_pad = next_pow2(n_leaves)`` leaves is the ``world`` subtrees
+    of ``n_pad / world`` leaves with ``log2 world`` levels of ``hash_pair`` on
+    top.  ``world`` must be a power of two no larger than ``n_pad``.
+    """
+    if n_leaves < 1:
+        raise ValueError("a tree needs at least one leaf")
+    if world < 1 or world & (world - 1):
+        raise ValueError("the number of ranks must be a power of two")
+    lp = (n_leaves - 1).bit_length()
+    top = (world - 1).bit_length()
+    if top > lp:
+        raise ValueError(f"{world} ranks exceed the {1 << lp} padded leaves of the tree")
+    sub = lp - top
+    size = 1 << sub
+    return [SplitRange(r, r * size, max(0, min(size, n_leaves - r * size)), sub, top) for r in range(world)]
+
+
+def split_view(view, rng: SplitRange):
+    """``view`` (this rank's rows of one sequence, local row 0 = position
+    ``rng.begin``) with the subtree fields set for ``commit.kv_commit``."""
+    from dataclasses import replace
+    return replace(view, seq_lens=[rng.count], pos_base=[rng.begin], tree_log2=rng.sub_log2)
+
+
+def combine_subtree_roots(ctx, gathered: torch.Tensor, n_layers: int, keep_trees: bool = False):
+    """Top levels of split trees: ``gathered`` is ``[world, n_layers, 32]``
+    (rank r's subtree roots); per layer, ``build_tree`` over the ``world``
+    subtree roots gives the layer's kv_root.  Returns ``(roots [n_layers, 32], top trees or None)``."""
+    from . import commit as C
+    world = gathered.shape[0]
+    leaves = gathered.permute(1, 0, 2).contiguous().view(-1, 32)      # [layer][rank]
+    return C.build_trees(ctx, leaves, [l * world for l in range(n_layers + 1)], keep_trees=keep_trees)
+
+
+def split_kv_commit(ctx, view, rng: SplitRange, n_layers: int, group=None, keep_trees: bool = False):
+    """Commit this rank's subtrees and exchange them: every rank gets the
+    request's ``kv_roots`` ``[n_layers, 32]``, equal to a single-GPU commit.
+
+    ``view`` holds this rank's rows (one sequence).  Returns
+    ``(kv_roots, local subtree TreeSet or None, top TreeSet or None)``.
+    """
+    from . import commit as C
+    if rng.count == 0 and rng.sub_log2 == 0:
+        # a single zero padding leaf (build_tree pads level 0 with [0; 32])
+        with torch.cuda.stream(ctx.stream):
+            local = torch.zeros(n_layers, 32, dtype=torch.uint8, device=f"cuda:{ctx.device}")
+        trees = None
+    else:
+        local, trees = C.kv_commit(ctx, split_view(view, rng), keep_trees=keep_trees)
+    world = dist.get_world_size(group)
+    with torch.cuda.stream(ctx.stream):
+        out = torch.empty(world * n_layers, 32, dtype=torch.uint8, device=local.device)
+        dist.all_gather_into_tensor(out, local.reshape(-1, 32).contiguous(), group=group)
+    roots, top = combine_subtree_roots(ctx, out.view(world, n_layers, 32), n_layers, keep_trees=keep_trees)
+    return roots, trees, top

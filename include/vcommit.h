@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define VC_ABI_VERSION 1
+#define VC_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define VC_API __attribute__((visibility("default")))
@@ -115,6 +115,18 @@ typedef struct vc_kv_desc {
                                          is reported by vc_ctx_sync as VC_ERANGE) */
     const void* const* k_layers;      /* HOST [n_layers] DEVICE base pointers */
     const void* const* v_layers;      /* HOST [n_layers] DEVICE base pointers */
+    /* Split trees: one request's trees spread over G GPUs, each holding the
+     * aligned range [r * 2^tree_log2, (r + 1) * 2^tree_log2) of positions
+     * (n_pad = G * 2^tree_log2, G a power of two).  Each GPU commits its
+     * subtrees; the all-gathered subtree roots, as the G leaves of one
+     * vc_build_trees tree per layer, give the merkle::build_tree roots
+     * (merkle.rs:11-48), since build_tree pads only level 0 with zeros. */
+    const int64_t* pos_base;          /* HOST [n_seqs] or NULL (0): position of the sequence's local row 0,
+                                         the u32 position hashed into hash_kv_entry */
+    int32_t tree_log2;                /* 0: every tree padded to the next power of two of seq_lens[s]
+                                         (build_tree); > 0: every tree is the subtree of 2^tree_log2 leaves,
+                                         the first seq_lens[s] real (0 allowed: a subtree of zero leaves,
+                                         root Z_tree_log2), the rest zero */
 } vc_kv_desc;
 
 /*
@@ -142,7 +154,8 @@ VC_API vc_status vc_kv_commit(vc_ctx* ctx, const vc_kv_desc* desc, uint8_t* kv_r
  * is a fixed 8 MiB device array inside the library (plus a small padding-root
  * table), held by every GPU that loads the library until the process exits.
  *
- * Same descriptor and output as vc_kv_commit, roots only (no tree set), on
+ * Same descriptor and output as vc_kv_commit (without split trees: pos_base
+ * and tree_log2 must be NULL / 0, VC_ENOTSUP otherwise), roots only (no tree set), on
  * the given stream (NULL = legacy default stream) of the current device.
  * Limits: at most 64 sequences and 256 layers per call, kv_dim and head_dim
  * multiples of 8, 16-byte aligned rows (VC_ENOTSUP otherwise), and

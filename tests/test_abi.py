@@ -27,7 +27,7 @@ def test_library_loads_and_exports_every_symbol():
     lib = _lib.lib()
     for s in header_symbols():
         assert hasattr(lib, s), s
-    assert lib.vc_abi_version() == 1
+    assert lib.vc_abi_version() == 2
 
 
 def test_last_error_is_empty_before_any_failure():

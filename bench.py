@@ -75,6 +75,13 @@ def algorithmic(w):
         return blocks, 0, leaves * kv * 16, leaves * (16 + 16 * kv), w["n_seqs"] * w["n_layers"]
     if w["kind"] == "kv":
         kv = w["n_heads"] * w["head_dim"]
+        if w.get("split"):
+            # split trees: this rank's range of the one sequence (aligned power of two)
+            from commitllm_b200.dist import split_ranges
+            rng = split_ranges(w["seq_len"], w["split"])[w.get("rank", 0)]
+            leaves = rng.count * w["n_layers"]
+            blocks = leaves * sha_blocks(16 + 16 * kv) + w["n_layers"] * tree_blocks(1 << rng.sub_log2)
+            return blocks, 0, leaves * kv * 4, leaves * (16 + 16 * kv), w["n_layers"]
         leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
         blocks = leaves * sha_blocks(16 + 16 * kv) + w["n_seqs"] * w["n_layers"] * tree_blocks(w["seq_len"])
         return blocks, 0, leaves * kv * 4, leaves * (16 + 16 * kv), w["n_seqs"] * w["n_layers"]
@@ -228,6 +235,39 @@ class KvStep:
             roots_host.copy_(roots.view(-1), non_blocking=True)
         trees.free()
         return roots.numel()
+
+
+class SplitKvStep:
+    """One request's KV trees split over the ranks by position (strong
+    scaling): each rank holds and commits its aligned range of positions,
+    the subtree roots are all-gathered, and every rank builds the top levels."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import dist as D
+        self.C, self.D, self.torch = C, D, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        if w["n_seqs"] != 1:
+            raise ValueError("split trees commit one sequence")
+        self.rng = D.split_ranges(w["seq_len"], world)[rank]
+        local = dict(w, seq_len=max(self.rng.count, 1))
+        self.view = make_view(local, device, seed=5000 + rank)     # this rank's rows only
+        self.launches = 3
+        self.kernel_events = []
+
+    def __call__(self, timed: bool):
+        torch = self.torch
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+        roots, trees, top = self.D.split_kv_commit(self.ctx, self.view, self.rng, self.w["n_layers"])
+        if timed:
+            e1.record(self.stream)
+            self.kernel_events.append((e0, e1))
+
+    def host_inputs(self):
+        return list(self.view.k_layers) + list(self.view.v_layers)
 
 
 # ---------------------------------------------------------------------------
@@ -558,9 +598,9 @@ def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
 
 
 def config_of(w, world):
-    c = {k: v for k, v in w.items() if k not in ("steps", "name", "kind")}
+    c = {k: v for k, v in w.items() if k not in ("steps", "name", "kind", "rank")}
     c["workload"] = w["name"]
-    c["parallelism"] = f"shard-by-sequence x{world}"
+    c["parallelism"] = f"split-trees x{world}" if w.get("split") else f"shard-by-sequence x{world}"
     return c
 
 
@@ -594,6 +634,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seqs", type=int, default=None, help="override the workload's sequence count")
     ap.add_argument("--layers", type=int, default=None, help="override the workload's layer count (small captures)")
+    ap.add_argument("--split-trees", action="store_true",
+                    help="N > 1: spread one request's trees over the ranks by position (strong scaling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = dict(WORKLOADS[args.workload])
@@ -623,7 +665,14 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     stream = torch.cuda.Stream(local)
     ctx = C.Context(local, stream)
-    step = {"kv": KvStep, "kvt": KvtStep, "trace": TraceStep}[w["kind"]](w, ctx, stream, local, rank, world)
+    if args.split_trees:
+        if w["kind"] != "kv" or w["n_seqs"] != 1:
+            raise SystemExit("--split-trees needs a one-sequence KV workload (c2)")
+        w = dict(w, split=world, rank=rank)
+        step = SplitKvStep(w, ctx, stream, local, rank, world)
+        args.no_e2e = True
+    else:
+        step = {"kv": KvStep, "kvt": KvtStep, "trace": TraceStep}[w["kind"]](w, ctx, stream, local, rank, world)
     torch.cuda.synchronize()
     blocks, other_blocks, src_bytes, msg_bytes, n_roots = algorithmic(w)
 
@@ -792,13 +841,17 @@ def main():
     alu_achieved = blocks * BLK_OPS / (k_avg * 1e-3) / 1e12
     alu_peak = peak_ops / 1e12
     hbm_achieved = src_bytes / (k_avg * 1e-3) / 1e9
+    # whole-job bytes: every rank its own transcript, or (split trees) one transcript over all ranks
+    job_bytes = (algorithmic({k: v for k, v in w.items() if k not in ("split", "rank")})[2] if w.get("split")
+                 else src_bytes * world)
     line = {
-        "metric": METRIC, "value": round(src_bytes * world / (ms_step * 1e-3) / 1e9, 3), "unit": "GB/s",
+        "metric": METRIC, "value": round(job_bytes / (ms_step * 1e-3) / 1e9, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if w.get("split") else "weak", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic",
         "config": dict(config_of(w, world), l2="inputs larger than L2 (%.0f MB per GPU)" % (src_bytes / 1e6)),
-        "roots_per_s": round(n_roots * world / (ms_step * 1e-3), 2),
-        "hashed_msg_GBps": round(msg_bytes * world / (ms_step * 1e-3) / 1e9, 3),
+        "roots_per_s": round((n_roots if w.get("split") else n_roots * world) / (ms_step * 1e-3), 2),
+        "hashed_msg_GBps": round(msg_bytes * (job_bytes / src_bytes) / (ms_step * 1e-3) / 1e9, 3),
         "roofline": {"bound": "int_alu", "achieved": round(alu_achieved, 3), "peak": round(alu_peak, 3),
                      "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4),
                      "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not (args.seqs or args.layers) else None,

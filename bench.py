@@ -48,6 +48,9 @@ WORKLOADS = {
     "c5": dict(kind="kv", name="llama3.1-70b-kv-shard", n_layers=80, n_heads=8, head_dim=128, n_seqs=4,
                seq_len=32768, paged=False, steps=8),
     # the reference's weight-provider path: KV recomputed from x_attn (compute_kv_transcript), then committed
+    # online per-step commit of a decode batch: 256 sequences, one token each per step (c4 shapes)
+    "online": dict(kind="online", name="llama3.1-8b-online-decode", n_layers=32, hidden=4096, n_seqs=256,
+                   vocab=128256, x_attn=True, steps=6),
     "c2t": dict(kind="kvt", name="llama3.1-8b-kv-transcript", n_layers=32, n_heads=8, head_dim=128, hidden=4096,
                 n_seqs=1, seq_len=4096, rope="llama3", steps=250),
 }
@@ -597,6 +600,104 @@ def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
     return per_tok * n_tok / dt / 1e9, threads, sample, dt
 
 
+def run_online(args, w, local):
+    """Online commit (OnlineCommitter.step) of a decode batch, alone and beside
+    a stream of bf16 GEMMs standing in for the model's forward pass."""
+    import torch
+    from commitllm_b200 import commit as C
+    from commitllm_b200.online import OnlineCommitter
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    L, H, V, B = w["n_layers"], w["hidden"], w["vocab"], w["n_seqs"]
+    stream = torch.cuda.Stream(local)
+    ctx = C.Context(local, stream)
+    n_steps = args.steps + args.warmup
+    oc = OnlineCommitter(ctx, max_slots=B, max_tokens=2 * n_steps + 4)
+    for s_ in range(B):
+        oc.open(s_, b"synthetic prompt %d" % s_, bytes([s_ % 256]) * 32, n_prompt_tokens=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4000)
+    a = torch.randint(-128, 128, (L, B, H), dtype=torch.int8, device=dev, generator=g)
+    x = torch.randint(-128, 128, (L, B, H), dtype=torch.int8, device=dev, generator=g)
+    sa = torch.rand(L, B, device=dev, generator=g) * 0.05 + 1e-3
+    logits = torch.randn(B, V, device=dev, generator=g) * 3.0
+    tok = torch.randint(0, V, (B,), dtype=torch.int32, device=dev, generator=g)
+    lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[B], tok_fwd=[0] * B, tok_row=list(range(B)),
+                        a_rows=[[a[l].data_ptr() for l in range(L)]], scale_a=[[sa[l].data_ptr() for l in range(L)]],
+                        scale_stride=1, x_attn_rows=[[x[l].data_ptr() for l in range(L)]],
+                        scale_x_attn=[[sa[l].data_ptr() for l in range(L)]], scale_x_stride=1,
+                        logits=logits, tok_logits_row=list(range(B)))
+    slots = list(range(B))
+    for _ in range(args.warmup):
+        oc.step(slots, lay, tok)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        clk.mark_start()
+        e0.record(stream)
+        for _ in range(args.steps):
+            oc.step(slots, lay, tok)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clk.mark_end()
+    ms = e0.elapsed_time(e1) / args.steps
+    # beside a model: bf16 GEMMs on another stream while one more step commits
+    A = torch.randn(8192, 8192, dtype=torch.bfloat16, device=dev)
+    Bm = torch.randn(8192, 8192, dtype=torch.bfloat16, device=dev)
+    gs = torch.cuda.Stream(local)
+    with torch.cuda.stream(gs):
+        for _ in range(3):
+            torch.matmul(A, Bm)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_g = 40
+    with torch.cuda.stream(gs):
+        s0.record(gs)
+        for _ in range(n_g):
+            torch.matmul(A, Bm)
+        s1.record(gs)
+    torch.cuda.synchronize()
+    g_alone = s0.elapsed_time(s1) / n_g
+    with torch.cuda.stream(gs):
+        s0.record(gs)
+    oc.step(slots, lay, tok)
+    with torch.cuda.stream(gs):
+        for _ in range(n_g):
+            torch.matmul(A, Bm)
+        s1.record(gs)
+    torch.cuda.synchronize()
+    g_with = s0.elapsed_time(s1) / n_g
+    for s_ in range(B):
+        oc.close(s_)
+    ctx.sync(600000)
+    per_tok = 14 + L * (H + 4 + 1 + (H + 4 if w["x_attn"] else 0)) + 21 + 32 + 4 * V
+    blocks = B * (sha_blocks(14 + L * (H + 4 + 1 + (H + 4 if w["x_attn"] else 0))) + sha_blocks(21 + 32 + 4 * V))
+    peak_ops = C.int_peak(ctx, 0, 4000)
+    achieved = blocks * BLK_OPS / (ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(B * per_tok / (ms * 1e-3) / 1e9, 3), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": w["name"], "n_layers": L, "hidden": H, "vocab": V, "sequences": B,
+                   "tokens_per_step": B, "x_attn": w["x_attn"], "l2": "inputs reused per step (%.0f MB)" %
+                   (B * per_tok / 1e6)},
+        "roofline": {"bound": "latency", "achieved": round(achieved, 3), "peak": round(peak_ops / 1e12, 3),
+                     "unit": "Tops/s", "frac": round(achieved / (peak_ops / 1e12), 4), "traffic": None,
+                     "kernel": "trace_leaf_kernel + io_chain_kernel",
+                     "note": "one thread per token: %d CTAs of %d SMs, each thread hashes %d serial blocks" %
+                             ((B + 127) // 128, ctx_sm(), blocks // B)},
+        "beside_gemm": {"gemm_ms_alone": round(g_alone, 3), "gemm_ms_with_online_step": round(g_with, 3),
+                        "gemm": "bf16 8192^3 on another stream"},
+        "gpu_launches": args.steps * 2, "clocks": clk.summary(), "e2e": None, "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def ctx_sm():
+    import torch
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+
+
 def config_of(w, world):
     c = {k: v for k, v in w.items() if k not in ("steps", "name", "kind", "rank")}
     c["workload"] = w["name"]
@@ -652,7 +753,16 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
+        if w["kind"] == "online":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no online per-step commit"}))
+            return
         run_reference(args, w, rank, world)
+        return
+    if w["kind"] == "online":
+        if world > 1:
+            raise SystemExit("the online workload runs on one GPU")
+        run_online(args, w, local)
         return
 
     import torch

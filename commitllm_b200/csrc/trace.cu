@@ -13,6 +13,12 @@ constexpr int kTraceThreads = 128;
 // 125.4 ms; the KV kernel, whose messages are half zero words, keeps the
 // plain compression (the split measured slower there).
 constexpr int kTraceSplit = kAddRound | kAddSched | kShrSched;
+// With few tokens (few CTAs per SM) each thread's hash is latency-bound and
+// the split's extra instructions cost more than the ALU relief gains: below
+// this many CTAs per SM the plain compression is used.  Measured (C4 message
+// shape, ms plain / split): 256 tokens 27.4 / 34.5, 1 CTA per SM 28.1 / 35.7,
+// 2 per SM 41.9 / 42.0, 4 per SM 81.9 / 74.3, 7 per SM 136.2 / 124.0.
+constexpr int kTraceSplitMinCtasPerSm = 3;
 
 // Domain separators (ASCII), merkle.rs:147, 179, 206, 233, 251, 555, 563, 574.
 __device__ const char kTagRetained[] = "vi-retained-v3";
@@ -25,6 +31,7 @@ __device__ const char kTagGenesis[] = "vi-io-genesis-v4";
 
 // One thread per token: hash_retained_state_direct (merkle.rs:144-161), then
 // the optional wraps of hash_retained_with_captured_logits (merkle.rs:170-241).
+template <int SPLIT>
 __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_constant__ TraceArgs a) {
   __shared__ uint32_t sbuf[16 * kTraceThreads];
   const int t = blockIdx.x * kTraceThreads + threadIdx.x;
@@ -32,7 +39,7 @@ __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_
   const int32_t* tk = a.tok + 5 * int64_t(t);
   const int f = tk[0];
   const int64_t row = tk[1];
-  Sha256Stream<kTraceThreads, kTraceSplit> s;
+  Sha256Stream<kTraceThreads, SPLIT> s;
   s.opq = &a.opq;  // parameter space (__grid_constant__): read as constant operands
   s.init(sbuf + threadIdx.x);
   s.put_tag(kTagRetained, 14);
@@ -165,9 +172,13 @@ __global__ void __launch_bounds__(kTraceThreads) tagged_hash_kernel(int n, int t
   store_digest(out + int64_t(i) * 32, s.h);
 }
 
-cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s) {
+cudaError_t launch_trace_leaves(const TraceArgs& a, int n_sm, cudaStream_t s) {
   if (a.n_tokens == 0) return cudaSuccess;
-  trace_leaf_kernel<<<(a.n_tokens + kTraceThreads - 1) / kTraceThreads, kTraceThreads, 0, s>>>(a);
+  const int grid = (a.n_tokens + kTraceThreads - 1) / kTraceThreads;
+  if (grid >= kTraceSplitMinCtasPerSm * n_sm)
+    trace_leaf_kernel<kTraceSplit><<<grid, kTraceThreads, 0, s>>>(a);
+  else
+    trace_leaf_kernel<0><<<grid, kTraceThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -104,7 +104,7 @@ struct TraceArgs {
   uint8_t* leaves;
   Opq opq;                      // multipliers of the balanced compression (make_opq())
 };
-cudaError_t launch_trace_leaves(const TraceArgs& a, cudaStream_t s);
+cudaError_t launch_trace_leaves(const TraceArgs& a, int n_sm, cudaStream_t s);
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
                             const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, uint8_t* prev_io,
                             cudaStream_t s);

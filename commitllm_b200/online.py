@@ -89,12 +89,17 @@ class OnlineCommitter:
         check(lib().vc_io_extend(ctx.handle, len(runs), C._i64(tok_off), ctypes.c_void_p(step_leaves.data_ptr()),
                                  ctypes.c_void_p(tok.data_ptr()), ctypes.c_void_p(prev.data_ptr()),
                                  ctypes.c_void_p(step_io.data_ptr())))
+        # each token's place in its request's history: one indexed scatter per buffer
+        row, col = [], []
+        for s, _i, k in runs:
+            row += [s] * k
+            col += range(self.count[s], self.count[s] + k)
         with torch.cuda.stream(ctx.stream):
             self.prev.index_copy_(0, idx, prev)
-            for s, i, k in runs:
-                c = self.count[s]
-                self.leaves[s, c:c + k].copy_(step_leaves[i:i + k])
-                self.io[s, c:c + k].copy_(step_io[i:i + k])
+            r = torch.tensor(row, dtype=torch.long).to(self.leaves.device, non_blocking=True)
+            c = torch.tensor(col, dtype=torch.long).to(self.leaves.device, non_blocking=True)
+            self.leaves[r, c] = step_leaves[:n]
+            self.io[r, c] = step_io
         for s, _i, k in runs:
             self.count[s] += k
 

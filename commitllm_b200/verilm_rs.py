@@ -328,6 +328,21 @@ class _Committed:
                 out += struct.pack("<IQ", p, layer.shape[1]) + layer[p].tobytes()
         return bytes(out)
 
+    def audit_v4(self, token_index: int, layer_indices=None, output_text=None, include_kv: bool = True) -> str:
+        """``audit_v4`` (verilm-py/src/lib.rs:681-712) builds a whole ``V4AuditResponse``,
+        whose shell openings replay the model's matrix products from the weights on
+        the CPU: verifier-side math outside this commitment library.  Its commitment
+        parts are here: ``retained_proof`` / ``io_proof`` and, for the KV fields,
+        ``audit_kv_json`` / ``audit_kv_bincode``."""
+        raise NotImplementedError("audit_v4 needs the shell openings (weight replay), which this GPU commit "
+                                  "library does not build; use retained_proof, io_proof and audit_kv_json")
+
+    def audit_v4_binary(self, token_index: int, layer_indices=None, output_text=None,
+                        include_kv: bool = True) -> bytes:
+        """See :meth:`audit_v4`; the binary form would be ``VV4A`` || zstd(bincode)."""
+        raise NotImplementedError("audit_v4_binary needs the shell openings (weight replay), which this GPU "
+                                  "commit library does not build; use audit_kv_bincode for the KV fields")
+
     def leaf_hashes(self) -> torch.Tensor:
         """The retained leaves (tree 0's level 0), a device view ``[n_tokens, 32]``."""
         return self._trees.nodes(0)[: self._n_tokens]

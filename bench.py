@@ -848,6 +848,27 @@ def main():
             io_chain["cpu_ms_one_chain"] = round((time.perf_counter() - t_c) * 1e3, 3)
         del leaves, tok, io_out
 
+    # openings: merkle::prove for 1 024 random (sequence, layer, position) leaves of one more commit
+    openings = None
+    if w["kind"] == "kv" and not w.get("split"):
+        import numpy as np
+        r_ = np.random.default_rng(99 + rank)
+        n_open = 1024
+        tr_ids = r_.integers(0, w["n_seqs"] * w["n_layers"], n_open).tolist()
+        lf_ids = r_.integers(0, w["seq_len"], n_open).tolist()
+        _, trees_o = C.kv_commit(ctx, step.view, keep_trees=True, roots_out=step.roots)
+        trees_o.prove(tr_ids[:8], lf_ids[:8])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        sib, depths = trees_o.prove(tr_ids, lf_ids)
+        b.record(stream)
+        torch.cuda.synchronize()
+        openings = {"n": n_open, "ms": round(a.elapsed_time(b), 3), "siblings_each": int(depths[0]),
+                    "what": "merkle::prove of random (sequence, layer, position) leaves, batched, device"}
+        del sib
+        trees_o.free()
+
     # integer-ALU peak probe on the same GPU, same run
     peak_ops = C.int_peak(ctx, 0, 4000)
     ctx.sync(timeout_ms=600000)
@@ -975,6 +996,7 @@ def main():
         "cpu_baseline": cpu,
         "e2e": e2e,
         "io_chain": io_chain,
+        "openings": openings,
         "transcript": transcript,
         "gpu_launches": args.steps * step.launches,
         "clocks": clk.summary(),

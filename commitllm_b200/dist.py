@@ -157,9 +157,16 @@ def split_kv_commit(ctx, view, rng: SplitRange, n_layers: int, group=None, keep_
         trees = None
     else:
         local, trees = C.kv_commit(ctx, split_view(view, rng), keep_trees=keep_trees)
-    world = dist.get_world_size(group)
     with torch.cuda.stream(ctx.stream):
-        out = torch.empty(world * n_layers, 32, dtype=torch.uint8, device=local.device)
-        dist.all_gather_into_tensor(out, local.reshape(-1, 32).contiguous(), group=group)
-    roots, top = combine_subtree_roots(ctx, out.view(world, n_layers, 32), n_layers, keep_trees=keep_trees)
+        gathered = gather_subtree_roots(local, n_layers, group)
+    roots, top = combine_subtree_roots(ctx, gathered, n_layers, keep_trees=keep_trees)
     return roots, trees, top
+
+
+def gather_subtree_roots(local: torch.Tensor, n_layers: int, group=None) -> torch.Tensor:
+    """The exchange of split trees: every rank's ``[n_layers, 32]`` subtree
+    roots, all-gathered into ``[world, n_layers, 32]`` in rank (= position) order."""
+    world = dist.get_world_size(group)
+    out = torch.empty(world * n_layers, 32, dtype=torch.uint8, device=local.device)
+    dist.all_gather_into_tensor(out, local.reshape(-1, 32).contiguous(), group=group)
+    return out.view(world, n_layers, 32)

@@ -92,3 +92,50 @@ def test_failed_rank_does_not_hang_the_others():
     res = _run(2, 2, 2, fail_rank=1, timeout=180)
     assert res[1][1] == "err" and "injected" in res[1][2]
     assert res[0][1] == "err"            # rank 0's collective ended with an error, not a hang
+
+
+def _split_worker(rank, world, port, n, L, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        from oracle import commit_oracle as O
+        from tests import kvref
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+        rng = D.split_ranges(n, world)[rank]
+        tr = kvref.contiguous(77, L, [n], 2, 8)
+        kf = [O.bf16_to_f64(tr.k[l].reshape(n, -1)) for l in range(L)]
+        vf = [O.bf16_to_f64(tr.v[l].reshape(n, -1)) for l in range(L)]
+        local = np.zeros((L, 32), np.uint8)
+        for l in range(L):
+            # this rank's subtree: its leaves, zero leaves past the end (the GPU commit in production)
+            lv = [O.hash_kv_entry(l, rng.begin + i, kf[l][rng.begin + i], vf[l][rng.begin + i]) if i < rng.count
+                  else bytes(32) for i in range(1 << rng.sub_log2)]
+            while len(lv) > 1:
+                lv = [O.hash_pair(lv[2 * i], lv[2 * i + 1]) for i in range(len(lv) // 2)]
+            local[l] = np.frombuffer(lv[0], np.uint8)
+        gathered = D.gather_subtree_roots(torch.from_numpy(local), L).numpy()
+        roots = [O.build_tree([bytes(gathered[r, l]) for r in range(world)]).root for l in range(L)]
+        full = [O.kv_tree_for_layer(l, kf[l], vf[l]).root for l in range(L)]
+        q.put((rank, "ok", roots == full, None))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, "err", f"{type(e).__name__}: {e}", traceback.format_exc()))
+
+
+@pytest.mark.parametrize("world,n", [(2, 37), (4, 100), (4, 9)])
+def test_split_tree_exchange_gives_single_process_roots(world, n):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_split_worker, args=(r, world, port, n, 3, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = sorted((q.get(timeout=120) for _ in range(world)), key=lambda x: x[0])
+    for p in ps:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert all(r[1] == "ok" and r[2] is True for r in res), res

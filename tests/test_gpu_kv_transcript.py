@@ -88,6 +88,8 @@ CASES = [
     (64, 2, 128, 3, 96, "mixed"),         # head_dim 96: 192-channel tiles, kv_dim 288
     (300, 1, 512, 8, 128, "tensor"),      # Llama-style kv_dim 1024
     (33, 2, 64, 2, 8, "tensor"),          # small heads: 8-wide RoPE groups
+    (160, 2, 3584, 4, 128, "channel_bias"),  # Qwen2.5-7B shapes: hidden 3584, 4 x 128 KV heads, biases
+    (129, 1, 8192, 8, 128, "tensor"),     # Llama-70B hidden 8192: 64 K-blocks per tile
 ]
 
 

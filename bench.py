@@ -670,6 +670,24 @@ def run_online(args, w, local):
     for s_ in range(B):
         oc.close(s_)
     ctx.sync(600000)
+    # deferred: 32 decode steps queued, then hashed in one launch (8 192 chains instead of 256)
+    n_def = 32
+    od = OnlineCommitter(ctx, max_slots=B, max_tokens=2 * n_def + 4, defer_tokens=B * n_def)
+    for s_ in range(B):
+        od.open(s_, b"synthetic prompt %d" % s_, bytes([s_ % 256]) * 32, n_prompt_tokens=1)
+    for _ in range(n_def):                       # warm-up round
+        od.step(slots, lay, tok)
+    torch.cuda.synchronize()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(n_def):
+        od.step(slots, lay, tok)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    ms_def = d0.elapsed_time(d1) / n_def
+    for s_ in range(B):
+        od.close(s_)
+    ctx.sync(600000)
     per_tok = 14 + L * (H + 4 + 1 + (H + 4 if w["x_attn"] else 0)) + 21 + 32 + 4 * V
     blocks = B * (sha_blocks(14 + L * (H + 4 + 1 + (H + 4 if w["x_attn"] else 0))) + sha_blocks(21 + 32 + 4 * V))
     peak_ops = C.int_peak(ctx, 0, 4000)
@@ -688,6 +706,9 @@ def run_online(args, w, local):
                              ((B + 127) // 128, ctx_sm(), blocks // B)},
         "beside_gemm": {"gemm_ms_alone": round(g_alone, 3), "gemm_ms_with_online_step": round(g_with, 3),
                         "gemm": "bf16 8192^3 on another stream"},
+        "deferred": {"steps_per_flush": n_def, "ms_per_step": round(ms_def, 3),
+                     "GBps": round(B * per_tok / (ms_def * 1e-3) / 1e9, 3),
+                     "note": "OnlineCommitter(defer_tokens=%d): the 32 steps' tokens hashed in one launch" % (B * n_def)},
         "gpu_launches": args.steps * 2, "clocks": clk.summary(), "e2e": None, "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)

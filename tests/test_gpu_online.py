@@ -19,7 +19,8 @@ pytestmark = pytest.mark.gpu
 L, H, V = 3, 40, 97
 
 
-def test_online_equals_offline(ctx):
+@pytest.mark.parametrize("defer", [0, 3, 1000])
+def test_online_equals_offline(ctx, defer):
     schedule = [  # per step: list of (slot, rows)
         [(0, 3), (1, 2)],
         [(0, 1), (1, 1)],
@@ -30,7 +31,8 @@ def test_online_equals_offline(ctx):
     closes = {2: [0], 3: [1], 4: [2]}            # slots closed after a step
     prompts = {0: b"alpha", 1: b"", 2: b"gamma prompt"}
     n_prompt = {0: 3, 1: 2, 2: 4}
-    oc = OnlineCommitter(ctx, max_slots=4, max_tokens=16)
+    oc = OnlineCommitter(ctx, max_slots=4, max_tokens=16, defer_tokens=defer)
+    held = []                                     # deferred passes are read at flush: keep captures alive
     hist = {s: [] for s in prompts}               # per slot: (a [L,H], scales [L], logits or None, token)
     results = {}
     rng = np.random.default_rng(5)
@@ -56,6 +58,7 @@ def test_online_equals_offline(ctx):
                 slots.append(s)
                 i += 1
         ad, sd = ctx.to_device(a), ctx.to_device(sc)
+        held.append((ad, sd))
         ld = ctx.to_device(np.stack(logits)) if logits else None
         lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[n], tok_fwd=[0] * n, tok_row=list(range(n)),
                             a_rows=[[ad.data_ptr() + l * n * H for l in range(L)]],

@@ -33,7 +33,9 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BLK_OPS = 1384          # int32 ops per SHA-256 block (one compression), see DESIGN.md
+# int32 ops per SHA-256 block (one compression): 64 rounds x (6 rotates + 4 logic + 4 adds)
+# + 48 schedule words x (6 shifts + 2 logic + 2 adds) + 8 final adds
+BLK_OPS = 1384
 METRIC = "trace bytes committed GB/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
 # kernel, from the ncu capture summarised in profiles/ (bytes, source)

@@ -39,7 +39,7 @@ BLK_OPS = 1384
 METRIC = "trace bytes committed GB/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
 # kernel, from the ncu capture summarised in profiles/ (bytes, source)
-TRAFFIC = {"c2": (560.3e6, "profiles/kv_commit_llama8b.md (ncu, same workload)")}
+TRAFFIC = {"c2": (559.0e6, "profiles/kv_commit_llama8b.md (ncu, same workload)")}
 WORKLOADS = {
     "c2": dict(kind="kv", name="llama3.1-8b-kv", n_layers=32, n_heads=8, head_dim=128, n_seqs=1, seq_len=4096,
                paged=False, steps=400),

@@ -7,6 +7,8 @@
   gathered into a contiguous layout (a size-independent property); a few
   trees are checked against the oracle directly; 1024 random openings verify
   against their roots.
+* Llama-3.1-70B sequence length (32 768 positions) and 32 769 (padded to
+  65 536): kv_roots against the C oracle, openings at both ends verify.
 """
 import numpy as np
 import pytest
@@ -71,3 +73,27 @@ def test_qwen7b_shape_paged_equals_contiguous_and_oracle(ctx):
         leaf = bytes(trees.nodes(t)[p].cpu().numpy())
         proof = O.MerkleProof(p, [bytes(x) for x in sib[i, :depth[i]]])
         assert O.verify(bytes(rp[t // L, t % L]), leaf, proof)
+
+
+@pytest.mark.parametrize("n", [32768, 32769])
+def test_llama70b_sequence_length_roots_and_deep_openings(ctx, n):
+    """C5's sequence length (32 768 positions: 256 chunks per tree, 15 levels)
+    and one more (padded to 65 536: half the tree is padding): kv_roots against
+    the oracle's C restatement, and openings at both ends verify."""
+    L, H, D = 2, 8, 128
+    k, v = synth.kv_rows_bf16(n % 97, L, n, H, D)
+    tr = kvref.Transcript(k, v, [n], VC_DTYPE_BF16)
+    view = tr.view(ctx.device)
+    roots, trees = C.kv_commit(ctx, view, keep_trees=True)
+    ctx.sync(timeout_ms=120000)
+    oroots, _ = tr.oracle(n_threads=L, with_nodes=False)
+    assert np.array_equal(roots.cpu().numpy(), oroots)
+    pos = [0, 1, n // 2, n - 2, n - 1]
+    sib, depth = trees.prove([1] * len(pos), pos)
+    sib = sib.cpu().numpy()
+    kf = O.bf16_to_f64(k[1].reshape(n, -1))
+    vf = O.bf16_to_f64(v[1].reshape(n, -1))
+    for i, p in enumerate(pos):
+        assert depth[i] == (n - 1).bit_length()
+        proof = O.MerkleProof(leaf_index=p, siblings=[bytes(x) for x in sib[i, :depth[i]]])
+        assert O.verify(bytes(oroots[0, 1]), O.hash_kv_entry(1, p, kf[p], vf[p]), proof)

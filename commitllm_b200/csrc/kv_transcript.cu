@@ -7,8 +7,9 @@
 // A tile is 128 positions x 256 channels of one layer's K or V projection:
 // TMA brings 128-byte K-slices of x_attn (A, 128 rows) and of the weight rows
 // (B, 256 rows) into shared memory (128-byte swizzle), one thread issues
-// tcgen05.mma kind::i8 into a 128 x 256 s32 accumulator in TMEM, and four
-// epilogue warps read it back (one position per thread) for the f64 values.
+// tcgen05.mma kind::i8 into a 128 x 256 s32 accumulator in TMEM, and eight
+// epilogue warps read it back (one position per thread, two warps per TMEM
+// lane quarter) for the f64 values.
 // i8 x i8 products summed in s32 are exact in any order, so the accumulators
 // equal matmul_i32 (crates/verilm-core/src/matmul.rs:12-22).  The epilogue
 // rounds every f64 operation separately (__dmul_rn / __dadd_rn: no fused

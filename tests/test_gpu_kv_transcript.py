@@ -90,6 +90,8 @@ CASES = [
     (33, 2, 64, 2, 8, "tensor"),          # small heads: 8-wide RoPE groups
     (160, 2, 3584, 4, 128, "channel_bias"),  # Qwen2.5-7B shapes: hidden 3584, 4 x 128 KV heads, biases
     (129, 1, 8192, 8, 128, "tensor"),     # Llama-70B hidden 8192: 64 K-blocks per tile
+    (70, 2, 512, 2, 256, "channel_bias"),  # head_dim 256 (the largest): one head per 256-channel tile
+    (1, 2, 128, 8, 128, "tensor"),        # a single position
 ]
 
 

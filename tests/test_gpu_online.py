@@ -19,8 +19,9 @@ pytestmark = pytest.mark.gpu
 L, H, V = 3, 40, 97
 
 
-@pytest.mark.parametrize("defer", [0, 3, 1000])
-def test_online_equals_offline(ctx, defer):
+@pytest.mark.parametrize("defer,ring", [(0, False), (3, False), (1000, False), (1000, True)])
+def test_online_equals_offline(ctx, defer, ring):
+    """ring: every pass writes its logits into one shared tensor (read in place at flush)."""
     schedule = [  # per step: list of (slot, rows)
         [(0, 3), (1, 2)],
         [(0, 1), (1, 1)],
@@ -36,6 +37,8 @@ def test_online_equals_offline(ctx, defer):
     hist = {s: [] for s in prompts}               # per slot: (a [L,H], scales [L], logits or None, token)
     results = {}
     rng = np.random.default_rng(5)
+    ring_t = ctx.empty(64, V, dtype=torch.float32) if ring else None
+    ring_used = 0
     for k, rows in enumerate(schedule):
         for s, _ in rows:
             if s not in oc.open_slots and not hist[s]:
@@ -60,6 +63,11 @@ def test_online_equals_offline(ctx, defer):
         ad, sd = ctx.to_device(a), ctx.to_device(sc)
         held.append((ad, sd))
         ld = ctx.to_device(np.stack(logits)) if logits else None
+        if ring and ld is not None:
+            ring_t[ring_used:ring_used + ld.shape[0]].copy_(ld)
+            logit_rows = [r + ring_used if r >= 0 else -1 for r in logit_rows]
+            ring_used += ld.shape[0]
+            ld = ring_t
         lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[n], tok_fwd=[0] * n, tok_row=list(range(n)),
                             a_rows=[[ad.data_ptr() + l * n * H for l in range(L)]],
                             scale_a=[[sd.data_ptr() + 4 * l * n for l in range(L)]], scale_stride=1,

@@ -76,10 +76,18 @@ def gather_roots(local: torch.Tensor, plan: List[Shard], n_seqs: int, n_layers: 
     world = len(plan)
     width = max(sh.n_trees for sh in plan)
     rank = dist.get_rank(group)
-    buf = torch.zeros(width, 32, dtype=torch.uint8, device=local.device)
-    buf[: plan[rank].n_trees].copy_(local.reshape(-1, 32))
+    uniform = all(sh.n_trees == width for sh in plan)
+    if uniform:
+        buf = local.reshape(-1, 32).contiguous()
+    else:
+        buf = torch.zeros(width, 32, dtype=torch.uint8, device=local.device)
+        buf[: plan[rank].n_trees].copy_(local.reshape(-1, 32))
     out = torch.empty(world * width, 32, dtype=torch.uint8, device=local.device)
     dist.all_gather_into_tensor(out, buf, group=group)
+    if uniform:
+        # shard_plan's shards tile the (sequence, layer) grid in row-major order, so
+        # without padding the gathered concatenation already is the result
+        return out.view(n_seqs, n_layers, 32)
     full = torch.empty(n_seqs, n_layers, 32, dtype=torch.uint8, device=local.device)
     for r, sh in enumerate(plan):
         got = out[r * width: r * width + sh.n_trees].view(sh.seq_end - sh.seq_begin, sh.layer_end - sh.layer_begin, 32)

@@ -35,6 +35,15 @@ def test_shard_plan_covers_every_tree_once():
         assert len(seen) == len(set(seen))
 
 
+def test_uniform_shard_plans_are_row_major():
+    """gather_roots returns the gathered buffer as is when every shard has the
+    same size: those plans must tile (sequence, layer) in row-major order."""
+    for S, L, W in [(1, 32, 8), (8, 4, 4), (32, 80, 8), (2, 6, 4), (4, 80, 8), (1, 32, 2)]:
+        plan = D.shard_plan(S, L, W)
+        if all(sh.n_trees == plan[0].n_trees for sh in plan):
+            assert D.tree_order(plan, L) == [(s, l) for s in range(S) for l in range(L)]
+
+
 def _worker(rank, world, port, S, L, fail_rank, q):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))

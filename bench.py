@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Trace-commitment throughput on B200 (trace bytes committed GB/s, + kv_roots/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c2t|c3|c4|c5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5|c2|c2t|c3|c4|online|request] [--impl ours|reference]
 
 A step is one pass of the commitment hot path over one batch of synthetic
 input already resident in HBM.
@@ -9,16 +9,26 @@ input already resident in HBM.
 KV workloads (bf16 K/V ~ N(0, 1), seeded): every (sequence, layer) tree is
 hashed -- leaf "vi-kv-v1" || u32 layer || u32 pos || f64(K) || f64(V),
 SHA-256 -- and reduced to its kv_root, nodes kept for openings.
-  c2  Llama-3.1-8B shape: 32 layers x 8 KV heads x 128, 1 sequence x 4096 tokens (default)
+  c5  Llama-3.1-70B shape: 80 layers x 8 x 128, 32 sequences x 32768 tokens, ONE job split over the
+      N GPUs by sequence (strong scaling; default).  A GPU's share (32/N sequences x 80 layers, up to
+      344 GB) does not fit HBM below N=4, so each GPU holds at most 8 distinct sequences x 80 layers
+      (86 GB) resident and commits its share in calls of up to 8 sequences; sequence s of a share
+      reads resident sequence s mod 8 (every leaf hashed, the same bytes re-read from HBM).  After
+      the last call the 2 560 kv_roots are all-gathered (NCCL) and the root-of-roots is built.
+  c2  Llama-3.1-8B shape: 32 layers x 8 KV heads x 128, 1 sequence x 4096 tokens
   c3  Qwen2.5-7B shape: 28 layers x 4 x 128, 16 sequences x 8192, paged 16-token blocks, permuted pages
-  c5  Llama-3.1-70B shape: 80 layers x 8 x 128, 4 sequences x 32768 per GPU (32 at 8 GPUs)
 Retained-state workload:
   c4  Llama-3.1-8B sampled decode: 256 sequences x 512 steps; per token 32 layers of a_i8[4096] +
       scale_a + x_attn_i8[4096] + scale_x_attn, and f32 captured logits[128256] ~ N(0, 3^2).
       A step = retained leaves of all 131 072 tokens, the 256 IO chains, the 512 trace/IO trees,
       prompt hashes and seed commitments.
-Every rank commits its own copy of the workload (weak scaling); at N > 1 the
-roots are all-gathered (NCCL) and the root-of-roots is built inside the step.
+Whole-request workload:
+  request  one c2-shaped request through verilm_rs.commit_minimal_from_captures: retained leaves with
+      the captured-logits wrap, the IO chain, the trace/IO trees and the 32 KV trees of its cache,
+      on overlapped streams.
+Except c5, every rank commits its own copy of the workload (weak scaling); at
+N > 1 the roots are all-gathered (NCCL) and the root-of-roots is built inside
+the step.
 """
 from __future__ import annotations
 
@@ -37,9 +47,6 @@ sys.path.insert(0, ROOT)
 # + 48 schedule words x (6 shifts + 2 logic + 2 adds) + 8 final adds
 BLK_OPS = 1384
 METRIC = "trace bytes committed GB/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
-# kernel, from the ncu capture summarised in profiles/ (bytes, source)
-TRAFFIC = {"c2": (559.0e6, "profiles/kv_commit_llama8b.md (ncu, same workload)")}
 WORKLOADS = {
     "c2": dict(kind="kv", name="llama3.1-8b-kv", n_layers=32, n_heads=8, head_dim=128, n_seqs=1, seq_len=4096,
                paged=False, steps=400),
@@ -47,8 +54,8 @@ WORKLOADS = {
                seq_len=8192, paged=True, steps=40),
     "c4": dict(kind="trace", name="llama3.1-8b-retained-logits", n_layers=32, hidden=4096, n_seqs=256,
                seq_len=512, vocab=128256, x_attn=True, steps=8),
-    "c5": dict(kind="kv", name="llama3.1-70b-kv-shard", n_layers=80, n_heads=8, head_dim=128, n_seqs=4,
-               seq_len=32768, paged=False, steps=8),
+    "c5": dict(kind="kv", name="llama3.1-70b-kv-32x32768", n_layers=80, n_heads=8, head_dim=128, n_seqs=32,
+               seq_len=32768, paged=False, job=True, resident_seqs=8, steps=8),
     # the reference's weight-provider path: KV recomputed from x_attn (compute_kv_transcript), then committed
     # online per-step commit of a decode batch: 256 sequences, one token each per step (c4 shapes)
     "online": dict(kind="online", name="llama3.1-8b-online-decode", n_layers=32, hidden=4096, n_seqs=256,
@@ -240,6 +247,70 @@ class KvStep:
             roots_host.copy_(roots.view(-1), non_blocking=True)
         trees.free()
         return roots.numel()
+
+
+class KvJobStep:
+    """One KV job split over the ranks by sequence (``dist.shard_plan``): rank
+    r commits its share of sequences x layers in calls of up to
+    ``resident_seqs`` sequences over the resident K/V (sequence s of the share
+    reads resident sequence s mod resident_seqs), keeping every tree for
+    openings; then the job's kv_roots are all-gathered and the root-of-roots
+    is built.  Every hash kernel of the job runs inside the step."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import dist as D
+        self.C, self.D, self.torch = C, D, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        self.plan = D.shard_plan(w["n_seqs"], w["n_layers"], world)
+        sh = self.plan[rank]
+        self.shard = sh
+        self.n_local = sh.seq_end - sh.seq_begin
+        self.n_layers_local = sh.layer_end - sh.layer_begin
+        self.resident = max(1, min(self.n_local, int(w.get("resident_seqs") or self.n_local)))
+        res = dict(w, n_seqs=self.resident, n_layers=self.n_layers_local)
+        self.view = make_view(res, device, seed=1000 + rank)
+        self.view.layer_base = sh.layer_begin
+        self.calls = [(b, min(self.resident, self.n_local - b)) for b in range(0, self.n_local, self.resident)]
+        self.roots = ctx.empty(self.n_local, self.n_layers_local, 32)
+        self.ror = ctx.empty(1, 32)
+        self.trees = []                  # [(first local sequence, count, TreeSet)] of the last step
+        self.kernel_events = []          # per call: (start, end) on the step stream
+        self.launches = len(self.calls) + (1 if world > 1 else 0)
+
+    def local_view(self, n):
+        from dataclasses import replace
+        return replace(self.view, seq_lens=list(self.view.seq_lens[:n]))
+
+    def __call__(self, timed: bool):
+        torch, C = self.torch, self.C
+        for _, _, ts in self.trees:      # last step's node blocks go back to the context's pool
+            ts.free()
+        self.trees = []
+        for b, n in self.calls:
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+            _, ts = C.kv_commit(self.ctx, self.local_view(n), keep_trees=True, roots_out=self.roots[b:b + n])
+            if timed:
+                e1.record(self.stream)
+                self.kernel_events.append((e0, e1))
+            self.trees.append((b, n, ts))
+        if self.world > 1:
+            with torch.cuda.stream(self.stream):
+                full = self.D.gather_roots(self.roots.view(-1, 32), self.plan, self.w["n_seqs"], self.w["n_layers"])
+                C.build_trees(self.ctx, full.view(-1, 32), [0, self.w["n_seqs"] * self.w["n_layers"]],
+                              keep_trees=False, roots_out=self.ror)
+
+    def locate(self, seq_local: int, layer_local: int):
+        for b, n, ts in self.trees:
+            if b <= seq_local < b + n:
+                return ts, (seq_local - b) * self.n_layers_local + layer_local
+        raise IndexError(seq_local)
+
+    def host_inputs(self):
+        return list(self.view.k_layers) + list(self.view.v_layers)
 
 
 class SplitKvStep:
@@ -464,13 +535,17 @@ class TraceStep:
 # ---------------------------------------------------------------------------
 
 def host_kv(w, seed, n_layers):
+    """bf16 K/V [n_layers, rows, heads, dim] on the host: one layer of N(0, 1)
+    values repeated over the layers (SHA-256 costs the same for any bytes; the
+    layer index in each leaf keeps the trees distinct)."""
     import numpy as np
     from tests import synth
     rows = w["n_seqs"] * w["seq_len"]
     rng = np.random.default_rng(seed)
-    shape = (n_layers, rows, w["n_heads"], w["head_dim"])
-    return (synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)),
-            synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32)))
+    shape = (rows, w["n_heads"], w["head_dim"])
+    k1 = synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))
+    v1 = synth.f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32))
+    return np.repeat(k1[None], n_layers, axis=0), np.repeat(v1[None], n_layers, axis=0)
 
 
 def cpu_kv(w, n_layers, n_threads, reps=1, seed=7):
@@ -580,15 +655,24 @@ def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
                   f"{kv_threads} thread(s)), oracle C restatement, extrapolated linearly to the workload")
         return src_full / total / 1e9, threads, sample, total
     if w["kind"] == "kv":
-        # the reference hashes KV trees in a sequential per-layer loop (prover/src/lib.rs:454-478)
-        threads = 1 if reference_threads else max(1, min(ncpu, w["n_seqs"] * w["n_layers"]))
-        layers = max(1, min(w["n_layers"], threads))
-        per = cpu_kv(w, layers, threads) / layers
-        layers = int(min(w["n_layers"], max(layers, budget_s * 0.5 / max(per, 1e-6))))
-        dt = cpu_kv(w, layers, threads, reps=reps)
-        src = src_full * layers / w["n_layers"]
-        sample = (f"{layers} of {w['n_layers']} layers x {w['n_seqs']} seq x {w['seq_len']} tokens, oracle C "
-                  f"restatement (OpenSSL SHA-256), {threads} thread(s) over trees")
+        # the reference hashes KV trees in a sequential per-layer loop (prover/src/lib.rs:454-478);
+        # every (sequence, layer) tree costs the same, so the sample is whole trees of one
+        # sequence (up to all its layers), extrapolated by tree count
+        n_trees = w["n_seqs"] * w["n_layers"]
+        w1 = dict(w, n_seqs=1, paged=False)
+        threads = 1 if reference_threads else max(1, min(ncpu, n_trees))
+        # at most ~2 GB of host K/V per sample
+        cap = max(1, min(w["n_layers"], int(2e9 // (4 * w["seq_len"] * w["n_heads"] * w["head_dim"]))))
+        layers = max(1, min(cap, threads))
+        per = cpu_kv(w1, layers, threads) / layers
+        layers = int(min(cap, max(layers, budget_s * 0.5 / max(per, 1e-6))))
+        if layers > threads:
+            layers -= layers % threads          # whole rounds of trees over the threads
+        dt = cpu_kv(w1, layers, threads, reps=reps)
+        src = src_full * layers / n_trees
+        sample = (f"{layers} of {n_trees} trees ({w['n_seqs']} seq x {w['n_layers']} layers) of {w['seq_len']} "
+                  f"tokens, oracle C restatement (OpenSSL SHA-256), {threads} thread(s) over trees, bytes per "
+                  f"second of the sample (every tree costs the same)")
         return src / dt / 1e9, threads, sample, dt
     # retained leaves: the reference uses rayon over tokens (prover/src/lib.rs:371-393), IO chain serial
     threads = ncpu
@@ -724,7 +808,12 @@ def ctx_sm():
 def config_of(w, world):
     c = {k: v for k, v in w.items() if k not in ("steps", "name", "kind", "rank")}
     c["workload"] = w["name"]
-    c["parallelism"] = f"split-trees x{world}" if w.get("split") else f"shard-by-sequence x{world}"
+    if w.get("split"):
+        c["parallelism"] = f"split-trees x{world}"
+    elif w.get("job"):
+        c["parallelism"] = f"one job, shard_plan by sequence x{world}"
+    else:
+        c["parallelism"] = f"every rank its own copy x{world}"
     return c
 
 
@@ -737,7 +826,8 @@ def run_reference(args, w, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": config_of(w, world),
+        "scaling": "strong" if (w.get("job") or args.split_trees) else "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic", "config": config_of(dict(w, split=world) if args.split_trees else w, world),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample + f", median of {reps} steps"},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -752,7 +842,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -804,10 +894,14 @@ def main():
         w = dict(w, split=world, rank=rank)
         step = SplitKvStep(w, ctx, stream, local, rank, world)
         args.no_e2e = True
+    elif w.get("job"):
+        step = KvJobStep(w, ctx, stream, local, rank, world)
     else:
         step = {"kv": KvStep, "kvt": KvtStep, "trace": TraceStep}[w["kind"]](w, ctx, stream, local, rank, world)
     torch.cuda.synchronize()
-    blocks, other_blocks, src_bytes, msg_bytes, n_roots = algorithmic(w)
+    # per-rank work of one step (a job's share, or this rank's copy)
+    w_rank = dict(w, n_seqs=step.n_local, n_layers=step.n_layers_local) if w.get("job") else w
+    blocks, other_blocks, src_bytes, msg_bytes, n_roots = algorithmic(w_rank)
 
     for _ in range(args.warmup):
         step(False)
@@ -821,8 +915,16 @@ def main():
 
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    # The clock sampler starts (and delivers its first row) before the ranks
+    # meet, and the timed region of every rank opens right after one device-side
+    # rendezvous on the step stream, so no rank starts its clock early.
     with Clocks(local) as clk:
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(torch.ones(1, device=f"cuda:{local}"))
         clk.mark_start()
         t0.record(stream)
         for _ in range(args.steps):
@@ -839,13 +941,14 @@ def main():
         dist.barrier()
     ms_step = total_ms / args.steps
     kms = [a.elapsed_time(b) for a, b in step.kernel_events]
-    k_avg = sum(kms) / len(kms)
+    k_avg = sum(kms) / len(kms)               # one launch of the dominant kernel
+    k_step = sum(kms) / args.steps            # all its launches of one step
 
     # the token-level IO chain of the KV workloads' sequences, timed on its own
     # (serial: one warp per sequence; not part of the KV step above)
     io_chain = None
     if w["kind"] in ("kv", "kvt"):
-        S, T = w["n_seqs"], w["seq_len"]
+        S, T = w_rank["n_seqs"], w["seq_len"]
         g = torch.Generator(device=f"cuda:{local}")
         g.manual_seed(77)
         leaves = torch.randint(0, 256, (S * T, 32), generator=g, device=f"cuda:{local}", dtype=torch.uint8)
@@ -873,7 +976,34 @@ def main():
 
     # openings: merkle::prove for 1 024 random (sequence, layer, position) leaves of one more commit
     openings = None
-    if w["kind"] == "kv" and not w.get("split"):
+    if w["kind"] == "kv" and w.get("job"):
+        # 1 024 random (sequence, layer, position) openings of this rank's trees of the last timed step
+        import numpy as np
+        r_ = np.random.default_rng(99 + rank)
+        n_open = 1024
+        seqs = r_.integers(0, step.n_local, n_open)
+        lays = r_.integers(0, step.n_layers_local, n_open)
+        poss = r_.integers(0, w["seq_len"], n_open)
+        groups = {}
+        for sq, ly, ps in zip(seqs, lays, poss):
+            ts, t = step.locate(int(sq), int(ly))
+            groups.setdefault(id(ts), (ts, [], []))[1].append(t)
+            groups[id(ts)][2].append(int(ps))
+        for ts, tl, pl in groups.values():
+            ts.prove(tl[:8], pl[:8])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        depth = 0
+        for ts, tl, pl in groups.values():
+            _, depths = ts.prove(tl, pl)
+            depth = int(depths[0])
+        b.record(stream)
+        torch.cuda.synchronize()
+        openings = {"n": n_open, "ms": round(a.elapsed_time(b), 3), "siblings_each": depth,
+                    "what": "merkle::prove of random (sequence, layer, position) leaves of the job's trees, batched, "
+                            "device"}
+    elif w["kind"] == "kv" and not w.get("split"):
         import numpy as np
         r_ = np.random.default_rng(99 + rank)
         n_open = 1024
@@ -937,6 +1067,17 @@ def main():
             estep = TraceStep(w_e, ctx, stream, local, rank, world=1)
             _, _, e_src, _, e_roots = algorithmic(w_e)
             e2e_note = "16 of 256 sequences per step (same shapes)"
+        elif w.get("job"):
+            # the job's share from pinned host memory would be up to 344 GB: the e2e leg
+            # commits the resident sequences x a layer slice (<= 4 GiB per step, same shapes)
+            w_s = dict(w_rank, n_seqs=step.resident, job=False)
+            src_s = algorithmic(w_s)[2]
+            n_l = max(1, min(w_s["n_layers"], int(w_s["n_layers"] * (4 << 30) // src_s)))
+            w_e = dict(w_s, n_layers=n_l)
+            estep = KvStep(w_e, ctx, stream, local, rank, world=1)
+            _, _, e_src, _, e_roots = algorithmic(w_e)
+            e2e_note = (f"{step.resident} of {w['n_seqs']} sequences x {n_l} of {w['n_layers']} layers per step "
+                        f"(same shapes)")
         elif src_bytes > (4 << 30):
             # keep the pinned host copy bounded: commit a layer slice of the same workload
             n_l = max(1, int(w["n_layers"] * (4 << 30) // src_bytes))
@@ -992,12 +1133,14 @@ def main():
     except OSError:
         pass
     hbm = peaks.get("hbm_gbs", 6650.0)
-    alu_achieved = blocks * BLK_OPS / (k_avg * 1e-3) / 1e12
+    alu_achieved = blocks * BLK_OPS / (k_step * 1e-3) / 1e12
     alu_peak = peak_ops / 1e12
-    hbm_achieved = src_bytes / (k_avg * 1e-3) / 1e9
-    # whole-job bytes: every rank its own transcript, or (split trees) one transcript over all ranks
-    job_bytes = (algorithmic({k: v for k, v in w.items() if k not in ("split", "rank")})[2] if w.get("split")
-                 else src_bytes * world)
+    hbm_achieved = src_bytes / (k_step * 1e-3) / 1e9
+    # whole-job bytes: one job over all ranks (c5, split trees), or every rank its own copy
+    strong = bool(w.get("split") or w.get("job"))
+    job_w = {k: v for k, v in w.items() if k not in ("split", "rank")}
+    job_bytes = algorithmic(job_w)[2] if strong else src_bytes * world
+    job_roots = algorithmic(job_w)[4] if strong else n_roots * world
     # the integer ALU pipe's own rate at the clock seen: 4 sub-partitions x 16 int32 lanes per clock per SM
     clocks = clk.summary()
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
@@ -1005,18 +1148,19 @@ def main():
     line = {
         "metric": METRIC, "value": round(job_bytes / (ms_step * 1e-3) / 1e9, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True, "scaling": "strong" if w.get("split") else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
         "dtype": "u8", "data": "synthetic",
-        "config": dict(config_of(w, world), l2="inputs larger than L2 (%.0f MB per GPU)" % (src_bytes / 1e6)),
-        "roots_per_s": round((n_roots if w.get("split") else n_roots * world) / (ms_step * 1e-3), 2),
+        "config": config_of(w, world),
+        "l2": "inputs larger than L2 (%.0f MB read per GPU per step)" % (src_bytes / 1e6),
+        "roots_per_s": round(job_roots / (ms_step * 1e-3), 2),
         "hashed_msg_GBps": round(msg_bytes * (job_bytes / src_bytes) / (ms_step * 1e-3) / 1e9, 3),
         "roofline": {"bound": "int_alu", "achieved": round(alu_achieved, 3), "peak": round(alu_peak, 3),
                      "unit": "Tops/s", "frac": round(alu_achieved / alu_peak, 4),
-                     "traffic": TRAFFIC[args.workload][0] if args.workload in TRAFFIC and not (args.seqs or args.layers) else None,
-                     "traffic_source": TRAFFIC[args.workload][1] if args.workload in TRAFFIC and not (args.seqs or args.layers) else None,
+                     "traffic": None,
                      "algorithmic_bytes": src_bytes,
                      "kernel": "trace_leaf_kernel" if w["kind"] == "trace" else "kv_commit_kernel",
-                     "kernel_ms": round(k_avg, 4), "sha_blocks": blocks, "ops_per_block": BLK_OPS,
+                     "kernel_ms": round(k_avg, 4), "launches_per_step": len(kms) // args.steps,
+                     "sha_blocks": blocks, "ops_per_block": BLK_OPS,
                      "peak_source": "vc_int_peak SHA-mix probe, this GPU, this run",
                      "alu_pipe": {"peak": round(pipe_peak, 3), "frac": round(alu_achieved / pipe_peak, 4),
                                   "source": "%d SMs x 64 int32 lanes/clk x median SM clock in the timed region; "

@@ -7,6 +7,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -56,11 +59,40 @@ int32_t vc::set_error(int32_t status, const char* fmt, ...) {
   return status;
 }
 
+namespace {
+
+// Node storage of released tree sets, kept for the next tree set of a
+// similar size so a steady commit loop allocates nothing.  Shared by a
+// context and the tree sets it made, so either may go first.  Blocks are
+// stream-ordered: a block released on the context's stream is reused by
+// later work on that stream only.
+struct NodePool {
+  std::mutex mu;
+  bool closed = false;
+  size_t cached = 0;
+  std::multimap<size_t, uint8_t*> free_blocks;   // capacity -> block
+  static constexpr size_t kMaxCached = size_t(16) << 30;
+};
+
+constexpr int kStageSlots = 16;  // descriptor uploads in flight before the host waits
+
+// One pinned staging buffer and the event that says its copy has been read.
+struct StageSlot {
+  char* p = nullptr;
+  size_t cap = 0;
+  cudaEvent_t done = nullptr;
+  bool pending = false;
+};
+
+}  // namespace
+
 struct vc_tree_set {
   int device = 0;
   cudaStream_t stream = nullptr;
   uint8_t* nodes = nullptr;
-  std::vector<int64_t> node_base;  // per tree
+  size_t bytes = 0;                 // capacity of `nodes`
+  std::shared_ptr<NodePool> pool;   // where `nodes` returns, or null
+  std::vector<int64_t> node_base;   // per tree
   std::vector<int64_t> n_leaves;
   std::vector<int32_t> log2_pad;
 };
@@ -72,12 +104,11 @@ struct vc_ctx {
   int* err = nullptr;               // device error flag
   uint8_t* scratch = nullptr;       // device, grow-only
   size_t scratch_cap = 0;
-  char* pinned = nullptr;           // host staging of descriptor tables
-  size_t pinned_cap = 0;
-  char* dargs = nullptr;            // device copy of the staged tables
+  StageSlot stage[kStageSlots];     // host staging of descriptor tables, a ring
+  int stage_next = 0;
+  char* dargs = nullptr;            // device copy of the staged tables (stream-ordered reuse)
   size_t dargs_cap = 0;
-  cudaEvent_t staged = nullptr;     // the last staging copy has been read
-  bool staged_pending = false;
+  std::shared_ptr<NodePool> pool;
   int n_sm = 0;
   double* rope = nullptr;           // device (cos, sin) table of the last RoPE frequencies
   int64_t rope_rows = 0;            // positions held
@@ -110,19 +141,25 @@ vc_status ensure_scratch(vc_ctx* c, size_t bytes) {
   return VC_OK;
 }
 
+// Copies the staged tables to the device argument buffer on the context's
+// stream.  The host copy goes through a ring of pinned slots, so the host
+// only waits when kStageSlots earlier uploads have not yet been read by the
+// GPU; the device buffer itself is reused in stream order.
 vc_status upload(vc_ctx* c, const Stager& st, char** dev) {
   const size_t n = std::max<size_t>(st.img.size(), 16);
-  if (c->staged_pending) {
-    VC_CUDA(cudaEventSynchronize(c->staged));
-    c->staged_pending = false;
+  StageSlot& sl = c->stage[c->stage_next];
+  c->stage_next = (c->stage_next + 1) % kStageSlots;
+  if (sl.pending) {
+    VC_CUDA(cudaEventSynchronize(sl.done));
+    sl.pending = false;
   }
-  if (n > c->pinned_cap) {
-    if (c->pinned) cudaFreeHost(c->pinned);
-    c->pinned = nullptr;
-    c->pinned_cap = 0;
+  if (n > sl.cap) {
+    if (sl.p) cudaFreeHost(sl.p);
+    sl.p = nullptr;
+    sl.cap = 0;
     const size_t cap = std::max(n, size_t(1) << 16);
-    if (cudaMallocHost(&c->pinned, cap) != cudaSuccess) return fail(VC_ENOMEM, "pinned staging of %zu bytes failed", cap);
-    c->pinned_cap = cap;
+    if (cudaMallocHost(&sl.p, cap) != cudaSuccess) return fail(VC_ENOMEM, "pinned staging of %zu bytes failed", cap);
+    sl.cap = cap;
   }
   if (n > c->dargs_cap) {
     VC_CUDA(cudaStreamSynchronize(c->stream));
@@ -133,10 +170,10 @@ vc_status upload(vc_ctx* c, const Stager& st, char** dev) {
     if (cudaMalloc(&c->dargs, cap) != cudaSuccess) return fail(VC_ENOMEM, "argument buffer of %zu bytes failed", cap);
     c->dargs_cap = cap;
   }
-  if (!st.img.empty()) std::memcpy(c->pinned, st.img.data(), st.img.size());
-  VC_CUDA(cudaMemcpyAsync(c->dargs, c->pinned, n, cudaMemcpyHostToDevice, c->stream));
-  VC_CUDA(cudaEventRecord(c->staged, c->stream));
-  c->staged_pending = true;
+  if (!st.img.empty()) std::memcpy(sl.p, st.img.data(), st.img.size());
+  VC_CUDA(cudaMemcpyAsync(c->dargs, sl.p, n, cudaMemcpyHostToDevice, c->stream));
+  VC_CUDA(cudaEventRecord(sl.done, c->stream));
+  sl.pending = true;
   *dev = c->dargs;
   return VC_OK;
 }
@@ -178,14 +215,31 @@ void plan_group(Plan& p, int64_t n, int n_layers, int64_t src_off, int seq, int6
   for (int j = 0; j < m.n_chunks; ++j) p.items.push_back(make_int2(mi, j));
 }
 
+// Node storage for a tree set: a released block of the context's pool whose
+// capacity is within 2x of the need, else a new stream-ordered allocation.
 vc_status make_tree_set(vc_ctx* c, const Plan& p, int n_layers, vc_tree_set** out) {
   auto* ts = new (std::nothrow) vc_tree_set();
   if (!ts) return fail(VC_ENOMEM, "tree set allocation failed");
   ts->device = c->device;
   ts->stream = c->stream;
-  if (cudaMallocAsync(reinterpret_cast<void**>(&ts->nodes), size_t(p.nodes) * 32, c->stream) != cudaSuccess) {
-    delete ts;
-    return fail(VC_ENOMEM, "tree node storage of %lld bytes failed", (long long)(p.nodes * 32));
+  ts->pool = c->pool;
+  const size_t need = std::max<size_t>(size_t(p.nodes) * 32, 256);
+  {
+    std::lock_guard<std::mutex> lk(c->pool->mu);
+    auto it = c->pool->free_blocks.lower_bound(need);
+    if (it != c->pool->free_blocks.end() && it->first <= 2 * need) {
+      ts->nodes = it->second;
+      ts->bytes = it->first;
+      c->pool->cached -= it->first;
+      c->pool->free_blocks.erase(it);
+    }
+  }
+  if (!ts->nodes) {
+    if (cudaMallocAsync(reinterpret_cast<void**>(&ts->nodes), need, c->stream) != cudaSuccess) {
+      delete ts;
+      return fail(VC_ENOMEM, "tree node storage of %zu bytes failed", need);
+    }
+    ts->bytes = need;
   }
   for (const TreeMeta& m : p.meta) {
     for (int l = 0; l < n_layers; ++l) {
@@ -240,7 +294,12 @@ vc_status vc_ctx_create(int32_t device, void* stream, vc_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->zero_roots, sizeof(uint32_t) * 8 * (kMaxTreeHeight + 1));
   if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemsetAsync(c->err, 0, sizeof(int), c->stream);
-  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->staged, cudaEventDisableTiming);
+  for (int i = 0; i < kStageSlots && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&c->stage[i].done, cudaEventDisableTiming);
+  if (e == cudaSuccess) {
+    c->pool = std::make_shared<NodePool>();
+    if (!c->pool) e = cudaErrorMemoryAllocation;
+  }
   if (e == cudaSuccess) e = launch_zero_roots(c->zero_roots, c->stream);
   if (e == cudaSuccess) {
     // Tree sets come from the stream-ordered pool: keep freed blocks cached.
@@ -266,8 +325,18 @@ vc_status vc_ctx_destroy(vc_ctx* c) {
   if (c->err) cudaFree(c->err);
   if (c->scratch) cudaFree(c->scratch);
   if (c->dargs) cudaFree(c->dargs);
-  if (c->pinned) cudaFreeHost(c->pinned);
-  if (c->staged) cudaEventDestroy(c->staged);
+  for (StageSlot& sl : c->stage) {
+    if (sl.p) cudaFreeHost(sl.p);
+    if (sl.done) cudaEventDestroy(sl.done);
+  }
+  if (c->pool) {
+    // Cached blocks go back now; tree sets still alive free their own later.
+    std::lock_guard<std::mutex> lk(c->pool->mu);
+    c->pool->closed = true;
+    for (auto& kv : c->pool->free_blocks) cudaFree(kv.second);
+    c->pool->free_blocks.clear();
+    c->pool->cached = 0;
+  }
   if (c->rope) cudaFree(c->rope);
   delete c;
   return VC_OK;
@@ -598,7 +667,18 @@ vc_status vc_tree_nodes(const vc_tree_set* ts, int32_t tree, const uint8_t** nod
 vc_status vc_tree_set_free(vc_tree_set* ts) {
   if (!ts) return VC_OK;
   DeviceGuard g(ts->device);
-  if (ts->nodes) cudaFreeAsync(ts->nodes, ts->stream);
+  if (ts->nodes) {
+    bool kept = false;
+    if (ts->pool) {
+      std::lock_guard<std::mutex> lk(ts->pool->mu);
+      if (!ts->pool->closed && ts->pool->cached + ts->bytes <= NodePool::kMaxCached) {
+        ts->pool->free_blocks.emplace(ts->bytes, ts->nodes);
+        ts->pool->cached += ts->bytes;
+        kept = true;
+      }
+    }
+    if (!kept) cudaFreeAsync(ts->nodes, ts->stream);
+  }
   delete ts;
   return VC_OK;
 }

@@ -239,11 +239,7 @@ template <> struct Chunk<2> {  // f64: 64 bytes
 
 // Message words of element i (0..7) of a chunk: w[2j] = bswap(lo32),
 // w[2j+1] = bswap(hi32).  `out` receives elements [e0, e0+n).
-template <int DT, bool FAST>
-__device__ __forceinline__ void chunk_words(const Chunk<DT>& c, int e0, int n, uint32_t* out);
-
-template <bool FAST>
-__device__ __forceinline__ void bf16_chunk_words(const Chunk<0>& c, int e0, int n, uint32_t* out) {
+__device__ __forceinline__ void chunk_words(const Chunk<0>& c, int e0, int n, uint32_t* out) {
   const uint32_t x[4] = {c.q.x, c.q.y, c.q.z, c.q.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -254,16 +250,7 @@ __device__ __forceinline__ void bf16_chunk_words(const Chunk<0>& c, int e0, int 
     if (2 * j + 1 < e0 + n) { out[2 * (2 * j + 1 - e0)] = 0; out[2 * (2 * j + 1 - e0) + 1] = w1; }
   }
 }
-template <>
-__device__ __forceinline__ void chunk_words<0, true>(const Chunk<0>& c, int e0, int n, uint32_t* out) {
-  bf16_chunk_words<true>(c, e0, n, out);
-}
-template <>
-__device__ __forceinline__ void chunk_words<0, false>(const Chunk<0>& c, int e0, int n, uint32_t* out) {
-  bf16_chunk_words<false>(c, e0, n, out);
-}
-template <bool FAST>
-__device__ __forceinline__ void f32_chunk_words(const Chunk<1>& c, int e0, int n, uint32_t* out) {
+__device__ __forceinline__ void chunk_words(const Chunk<1>& c, int e0, int n, uint32_t* out) {
   const uint32_t x[8] = {c.q[0].x, c.q[0].y, c.q[0].z, c.q[0].w, c.q[1].x, c.q[1].y, c.q[1].z, c.q[1].w};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -274,16 +261,7 @@ __device__ __forceinline__ void f32_chunk_words(const Chunk<1>& c, int e0, int n
     out[2 * (i - e0) + 1] = bswap32(hi);
   }
 }
-template <>
-__device__ __forceinline__ void chunk_words<1, true>(const Chunk<1>& c, int e0, int n, uint32_t* out) {
-  f32_chunk_words<true>(c, e0, n, out);
-}
-template <>
-__device__ __forceinline__ void chunk_words<1, false>(const Chunk<1>& c, int e0, int n, uint32_t* out) {
-  f32_chunk_words<false>(c, e0, n, out);
-}
-template <bool FAST>
-__device__ __forceinline__ void f64_chunk_words(const Chunk<2>& c, int e0, int n, uint32_t* out) {
+__device__ __forceinline__ void chunk_words(const Chunk<2>& c, int e0, int n, uint32_t* out) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     if (i < e0 || i >= e0 + n) continue;
@@ -294,35 +272,13 @@ __device__ __forceinline__ void f64_chunk_words(const Chunk<2>& c, int e0, int n
     out[2 * (i - e0) + 1] = bswap32(hi);
   }
 }
-template <>
-__device__ __forceinline__ void chunk_words<2, true>(const Chunk<2>& c, int e0, int n, uint32_t* out) {
-  f64_chunk_words<true>(c, e0, n, out);
-}
-template <>
-__device__ __forceinline__ void chunk_words<2, false>(const Chunk<2>& c, int e0, int n, uint32_t* out) {
-  f64_chunk_words<false>(c, e0, n, out);
-}
-
-template <int DT>
-__device__ __forceinline__ uint32_t chunk_special(const Chunk<DT>& c);
-template <>
-__device__ __forceinline__ uint32_t chunk_special<0>(const Chunk<0>& c) { return 0; }  // widening is exact
-template <>
-__device__ __forceinline__ uint32_t chunk_special<1>(const Chunk<1>& c) { return 0; }
-template <>
-__device__ __forceinline__ uint32_t chunk_special<2>(const Chunk<2>& c) { return 0; }
 
 // One block = the last 2 elements of the previous chunk + the first 6 of
 // the current one (the 16-byte leaf prefix shifts f64 slots by two).
 template <int DT>
 __device__ __forceinline__ void block_words(const Chunk<DT>& prev, const Chunk<DT>& cur, uint32_t w[16]) {
-  if (chunk_special<DT>(prev) | chunk_special<DT>(cur)) {
-    chunk_words<DT, false>(prev, 6, 2, w);
-    chunk_words<DT, false>(cur, 0, 6, w + 4);
-  } else {
-    chunk_words<DT, true>(prev, 6, 2, w);
-    chunk_words<DT, true>(cur, 0, 6, w + 4);
-  }
+  chunk_words(prev, 6, 2, w);
+  chunk_words(cur, 0, 6, w + 4);
 }
 
 // hash_kv_entry (merkle.rs:285-293) of one (layer, position) with
@@ -340,11 +296,7 @@ __device__ __forceinline__ void kv_leaf(uint32_t st[8], uint32_t layer, uint32_t
   w[1] = 0x762d7631u;  // "v-v1"
   w[2] = bswap32(layer);
   w[3] = bswap32(pos);
-  if (chunk_special<DT>(cur)) {
-    chunk_words<DT, false>(cur, 0, 6, w + 4);
-  } else {
-    chunk_words<DT, true>(cur, 0, 6, w + 4);
-  }
+  chunk_words(cur, 0, 6, w + 4);
   compress(st, w);
   for (int b = 1; b < n_chunks; ++b) {
     prev = cur;
@@ -354,11 +306,7 @@ __device__ __forceinline__ void kv_leaf(uint32_t st[8], uint32_t layer, uint32_t
     compress(st, w);
   }
   // Last block: elements 2*kv-2, 2*kv-1, then 0x80, zeros, bit length.
-  if (chunk_special<DT>(cur)) {
-    chunk_words<DT, false>(cur, 6, 2, w);
-  } else {
-    chunk_words<DT, true>(cur, 6, 2, w);
-  }
+  chunk_words(cur, 6, 2, w);
   w[4] = 0x80000000u;
 #pragma unroll
   for (int i = 5; i < 15; ++i) w[i] = 0;
@@ -662,6 +610,12 @@ extern "C" vc_status vc_kv_commit_noalloc(const vc_kv_desc* d, uint8_t* kv_roots
   const bool paged = d->block_tables != nullptr;
   if (paged && (d->block_size < 1 || d->max_blocks_per_seq < 1))
     return set_error(VC_EINVAL, "vc_kv_commit_noalloc: paged layout needs block_size and max_blocks_per_seq >= 1");
+  // A page id from the device block table is only checked on the GPU; without
+  // a flag to report a bad one, its leaf would hash as zeros and the call
+  // would return a wrong root as success.
+  if (paged && !err_flag_dev)
+    return set_error(VC_EINVAL, "vc_kv_commit_noalloc: a paged layout needs err_flag_dev (bad page ids are "
+                                "only detected on the device)");
   bool fast = kv % 8 == 0 && d->head_dim % 8 == 0 && (d->stride_row * esz) % 16 == 0 &&
               (d->stride_head * esz) % 16 == 0 && (!paged || (d->stride_page * esz) % 16 == 0);
   for (int l = 0; l < d->n_layers && fast; ++l)
@@ -739,6 +693,7 @@ extern "C" vc_status vc_kv_commit_noalloc(const vc_kv_desc* d, uint8_t* kv_roots
   a.paged = paged ? 1 : 0;
   a.cache_elems = d->cache_elems;
   a.row_span = row_span;
+  // Contiguous rows were all checked above, so the internal word is never set for them.
   a.err = err_flag_dev ? err_flag_dev : reinterpret_cast<int*>(scratch);
   a.out.nodes = nullptr;
   a.out.counters = reinterpret_cast<uint32_t*>(scratch + kNoAllocErrBytes);

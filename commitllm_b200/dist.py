@@ -66,6 +66,12 @@ def tree_order(plan: List[Shard], n_layers: int) -> List[Tuple[int, int]]:
     return order
 
 
+def _row_major(plan: List[Shard], n_seqs: int, n_layers: int) -> bool:
+    """True when the shards, concatenated in rank order, are the (sequence,
+    layer) grid in row-major order: then the gathered buffer needs no reordering."""
+    return tree_order(plan, n_layers) == [(s, l) for s in range(n_seqs) for l in range(n_layers)]
+
+
 def gather_roots(local: torch.Tensor, plan: List[Shard], n_seqs: int, n_layers: int,
                  group=None) -> torch.Tensor:
     """All-gather every rank's ``[n_trees_r, 32]`` roots into ``[n_seqs, n_layers, 32]``.
@@ -76,7 +82,7 @@ def gather_roots(local: torch.Tensor, plan: List[Shard], n_seqs: int, n_layers: 
     world = len(plan)
     width = max(sh.n_trees for sh in plan)
     rank = dist.get_rank(group)
-    uniform = all(sh.n_trees == width for sh in plan)
+    uniform = all(sh.n_trees == width for sh in plan) and _row_major(plan, n_seqs, n_layers)
     if uniform:
         buf = local.reshape(-1, 32).contiguous()
     else:

@@ -161,9 +161,11 @@ VC_API vc_status vc_kv_commit(vc_ctx* ctx, const vc_kv_desc* desc, uint8_t* kv_r
  * multiples of 8, 16-byte aligned rows (VC_ENOTSUP otherwise), and
  * 256 + 4 * n_trees (rounded up to 256) + 32 * (sum over trees of
  * padded_size / 128) bytes of scratch <= 8 MiB (VC_EINVAL otherwise).
- * err_flag_dev: optional DEVICE int set to 1 when a paged row falls outside
- * cache_elems (the caller clears it); NULL ignores such rows silently after
- * zero-hashing them.
+ * err_flag_dev: DEVICE int set to 1 when a paged row (a negative page id or
+ * one past cache_elems in the device block table) falls outside the cache;
+ * the caller clears it before the call and reads it after.  The roots of a
+ * call that set it are void.  Required for a paged layout (VC_EINVAL when
+ * NULL); contiguous rows are checked on the host, and may pass NULL.
  * The first call on a device looks up the scratch address and fills the
  * padding-root table, synchronising the stream once: make that first call
  * before any stream capture.  Every call shares the one scratch array, so

@@ -292,6 +292,153 @@ def io_chain(trace_leaves: Sequence[bytes], token_ids: Sequence[int], prompt: by
 
 
 # ---------------------------------------------------------------------------
+# Four-spec manifest hashing: merkle.rs:324-457, specs from the flat manifest
+# by DeploymentManifest::split (types.rs:512-520, From impls 574-775).
+# A manifest here is a dict of the Rust field names; [u8; 32] as bytes,
+# Option as None, Vec<(u32, f32)> as a list of pairs.
+# ---------------------------------------------------------------------------
+
+def _opt32(h, v):
+    """hash_optional_32 (merkle.rs:459-467)."""
+    if v is None:
+        h.update(b"\x00")
+    else:
+        h.update(b"\x01")
+        h.update(v)
+
+
+def _opt_u32(h, v):
+    """hash_optional_u32 (merkle.rs:469-477)."""
+    if v is None:
+        h.update(b"\x00")
+    else:
+        h.update(b"\x01")
+        h.update(struct.pack("<I", v))
+
+
+def _opt_f64(h, v):
+    """hash_optional_f64 (merkle.rs:479-487)."""
+    if v is None:
+        h.update(b"\x00")
+    else:
+        h.update(b"\x01")
+        h.update(struct.pack("<d", v))
+
+
+def _opt_str(h, v):
+    """hash_optional_string (merkle.rs:489-498)."""
+    if v is None:
+        h.update(b"\x00")
+    else:
+        b = v.encode()
+        h.update(b"\x01")
+        h.update(struct.pack("<I", len(b)))
+        h.update(b)
+
+
+def hash_input_spec(m) -> bytes:
+    """``hash_input_spec`` (merkle.rs:324-335)."""
+    h = hashlib.sha256(b"vi-input-v1")
+    h.update(m["tokenizer_hash"])
+    _opt32(h, m["system_prompt_hash"])
+    _opt32(h, m["chat_template_hash"])
+    _opt_str(h, m["bos_eos_policy"])
+    _opt_str(h, m["truncation_policy"])
+    _opt_str(h, m["special_token_policy"])
+    _opt_str(h, m["padding_policy"])
+    return h.digest()
+
+
+def hash_model_spec(m) -> bytes:
+    """``hash_model_spec`` (merkle.rs:338-367)."""
+    h = hashlib.sha256(b"vi-model-v1")
+    _opt32(h, m["weight_hash"])
+    _opt32(h, m["quant_hash"])
+    _opt32(h, m["rope_config_hash"])
+    if m["rmsnorm_eps"] is not None:
+        h.update(b"\x01")
+        h.update(struct.pack("<d", m["rmsnorm_eps"]))
+    else:
+        h.update(b"\x00")
+    _opt32(h, m["adapter_hash"])
+    _opt_u32(h, m["n_layers"])
+    _opt_u32(h, m["hidden_dim"])
+    _opt_u32(h, m["vocab_size"])
+    _opt32(h, m["embedding_merkle_root"])
+    _opt_str(h, m["quant_family"])
+    _opt_str(h, m["scale_derivation"])
+    _opt_u32(h, m["quant_block_size"])
+    _opt_u32(h, m["kv_dim"])
+    _opt_u32(h, m["ffn_dim"])
+    _opt_u32(h, m["d_head"])
+    _opt_u32(h, m["n_q_heads"])
+    _opt_u32(h, m["n_kv_heads"])
+    _opt_f64(h, m["rope_theta"])
+    return h.digest()
+
+
+def hash_decode_spec(m) -> bytes:
+    """``hash_decode_spec`` (merkle.rs:370-401)."""
+    h = hashlib.sha256(b"vi-decode-v1")
+    h.update(struct.pack("<f", m["temperature"]))
+    h.update(struct.pack("<I", m["top_k"]))
+    h.update(struct.pack("<f", m["top_p"]))
+    h.update(struct.pack("<f", m["repetition_penalty"]))
+    h.update(struct.pack("<f", m["frequency_penalty"]))
+    h.update(struct.pack("<f", m["presence_penalty"]))
+    h.update(struct.pack("<I", len(m["logit_bias"])))
+    for tok, bias in m["logit_bias"]:
+        h.update(struct.pack("<I", tok))
+        h.update(struct.pack("<f", bias))
+    h.update(struct.pack("<I", len(m["bad_word_ids"])))
+    for tok in m["bad_word_ids"]:
+        h.update(struct.pack("<I", tok))
+    g = m["guided_decoding"].encode()
+    h.update(struct.pack("<I", len(g)))
+    h.update(g)
+    if m["sampler_version"] is not None:
+        sv = m["sampler_version"].encode()
+        h.update(b"\x01")
+        h.update(struct.pack("<I", len(sv)))
+        h.update(sv)
+    else:
+        h.update(b"\x00")
+    _opt_str(h, m["decode_mode"])
+    return h.digest()
+
+
+def hash_output_spec(m) -> bytes:
+    """``hash_output_spec`` (merkle.rs:404-427)."""
+    h = hashlib.sha256(b"vi-output-v1")
+    h.update(m["eos_policy"].encode())
+    h.update(struct.pack("<I", len(m["stop_sequences"])))
+    for st in m["stop_sequences"]:
+        b = st.encode()
+        h.update(struct.pack("<I", len(b)))
+        h.update(b)
+    h.update(struct.pack("<I", m["max_tokens"]))
+    h.update(struct.pack("<I", m["min_tokens"]))
+    h.update(bytes([1 if m["ignore_eos"] else 0]))
+    _opt_str(h, m["detokenization_policy"])
+    if m["eos_token_id"] is not None:
+        h.update(bytes([1]))
+        h.update(struct.pack("<I", m["eos_token_id"]))
+    else:
+        h.update(bytes([0]))
+    return h.digest()
+
+
+def hash_manifest_composed(h_input: bytes, h_model: bytes, h_decode: bytes, h_output: bytes) -> bytes:
+    """``hash_manifest_composed`` (merkle.rs:432-446)."""
+    return sha256(b"vi-manifest-v4", h_input, h_model, h_decode, h_output)
+
+
+def hash_manifest(m) -> bytes:
+    """``hash_manifest`` (merkle.rs:452-457)."""
+    return hash_manifest_composed(hash_input_spec(m), hash_model_spec(m), hash_decode_spec(m), hash_output_spec(m))
+
+
+# ---------------------------------------------------------------------------
 # commit_minimal: crates/verilm-prover/src/lib.rs:336-499 (hashing parts)
 # ---------------------------------------------------------------------------
 

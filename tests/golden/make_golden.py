@@ -1,9 +1,9 @@
 """Regenerate ``reference_pins.json`` from the reference's own test data.
 
-Run in a container that has the reference checked out (read-only) at
-``/root/reference``::
+Run in a container that has the reference checked out (read-only); its
+root is a required argument::
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 What it extracts (all read as data, nothing of the reference is executed):
 
@@ -15,10 +15,16 @@ What it extracts (all read as data, nothing of the reference is executed):
   ``V4AuditResponse`` (types.rs:1475-1502) and ``BatchCommitment``
   (types.rs:1710-1759).  Their file SHA-256 is pinned by
   ``crates/verilm-verify/tests/cross_version.rs:431-442``.
+  The whole receipt is decoded (through ``witnessed_scores``, the last field,
+  to the end of the buffer); the decompressed bincode is kept as hex so that
+  a bincode writer can be checked byte for byte, and the fullbridge receipt's
+  ``manifest`` pins the four-spec hashes its commitment carries.
 * The golden hex pins of ``golden_e2e_verify``
   (``crates/verilm-test-vectors/tests/golden_conformance.rs:206-261``): the
   same toy model (seed 12345, input 0..16) as the canonical fixture, prompt
   ``b"golden test"``, token 42.
+* ``golden_manifest`` and its pinned ``hash_manifest`` / ``hash_model_spec``
+  hex (``golden_conformance.rs:132-201``), read from the Rust struct literal.
 
 The prompts and token ids are the inputs written in those two test files.
 """
@@ -28,6 +34,7 @@ import ctypes
 import hashlib
 import json
 import os
+import re
 import struct
 import sys
 
@@ -95,12 +102,23 @@ class Bincode:
     def bytes_vec(self):
         return self.take(self.u64())
 
+    def bytes_vec_f64(self):
+        n = self.u64()
+        return self.take(8 * n).hex()
+
 
 def read_proof(r: Bincode):
     return {"leaf_index": r.u32(), "siblings": [s.hex() for s in r.vec(r.arr32)]}
 
 
-def read_v4_audit_prefix(blob: bytes):
+def _prefix_len(blob: bytes) -> int:
+    """Bytes of the decompressed receipt that read_v4_audit_prefix consumes."""
+    holder = {}
+    read_v4_audit_prefix(blob, holder)
+    return holder["end"]
+
+
+def read_v4_audit_prefix(blob: bytes, _end=None):
     if blob[:4] != b"VV4A":
         raise ValueError("not a VV4A receipt")
     r = Bincode(zstd_decompress(blob[4:]))
@@ -139,7 +157,154 @@ def read_v4_audit_prefix(blob: bytes):
     c["kv_roots"] = [x.hex() for x in r.vec(r.arr32)]
     out["commitment"] = c
     out["revealed_seed"] = r.arr32().hex()
+    if _end is not None:
+        _end["end"] = r.o
     return out
+
+
+def _b32(r):
+    return r.arr32().hex()
+
+
+def read_manifest(r: Bincode):
+    """DeploymentManifest (types.rs:335-505), fields in declaration order."""
+    f32 = lambda: struct.unpack("<f", r.take(4))[0]
+    f64 = lambda: struct.unpack("<d", r.take(8))[0]
+    text = lambda: r.bytes_vec().decode()
+    m = {}
+    m["tokenizer_hash"] = _b32(r)
+    m["temperature"] = f32()
+    m["top_k"] = r.u32()
+    m["top_p"] = f32()
+    m["eos_policy"] = text()
+    for k in ("weight_hash", "quant_hash", "system_prompt_hash"):
+        m[k] = r.option(lambda: _b32(r))
+    for k in ("repetition_penalty", "frequency_penalty", "presence_penalty"):
+        m[k] = f32()
+    m["logit_bias"] = r.vec(lambda: [r.u32(), f32()])
+    m["bad_word_ids"] = r.vec(r.u32)
+    m["guided_decoding"] = text()
+    m["stop_sequences"] = r.vec(text)
+    m["max_tokens"] = r.u32()
+    m["chat_template_hash"] = r.option(lambda: _b32(r))
+    m["rope_config_hash"] = r.option(lambda: _b32(r))
+    m["rmsnorm_eps"] = r.option(f64)
+    for k in ("sampler_version", "decode_mode", "bos_eos_policy", "truncation_policy", "special_token_policy",
+              "padding_policy"):
+        m[k] = r.option(text)
+    m["adapter_hash"] = r.option(lambda: _b32(r))
+    for k in ("n_layers", "hidden_dim", "vocab_size"):
+        m[k] = r.option(r.u32)
+    m["embedding_merkle_root"] = r.option(lambda: _b32(r))
+    m["quant_family"] = r.option(text)
+    m["scale_derivation"] = r.option(text)
+    m["quant_block_size"] = r.option(r.u32)
+    m["attn_backend"] = r.option(text)
+    m["attn_dtype"] = r.option(text)
+    for k in ("kv_dim", "ffn_dim", "d_head", "n_q_heads", "n_kv_heads"):
+        m[k] = r.option(r.u32)
+    m["rope_theta"] = r.option(f64)
+    m["min_tokens"] = r.u32()
+    m["ignore_eos"] = bool(r.u8())
+    m["detokenization_policy"] = r.option(text)
+    m["eos_token_id"] = r.option(r.u32)
+    return m
+
+
+def _i32_vec(r):
+    n = r.u64()
+    return list(struct.unpack(f"<{n}i", r.take(4 * n)))
+
+
+def _f32_vec(r):
+    n = r.u64()
+    return list(struct.unpack(f"<{n}f", r.take(4 * n)))
+
+
+def read_shell_opening(r: Bincode):
+    """ShellTokenOpening (types.rs:1378-1397) with its ShellLayerOpenings (1345-1364)."""
+    def layer():
+        d = {k: _i32_vec(r) for k in ("attn_out", "g", "u", "ffn_out")}
+        for k in ("q", "k", "v"):
+            d[k] = r.option(lambda: _i32_vec(r))
+        for k in ("scale_x_attn", "scale_x_ffn", "scale_h"):
+            d[k] = struct.unpack("<f", r.take(4))[0]
+        return d
+    o = {"layers": r.vec(layer)}
+    o["layer_indices"] = r.option(lambda: r.vec(r.u64))
+    o["initial_residual"] = r.option(lambda: _f32_vec(r))
+    o["embedding_proof"] = r.option(lambda: read_proof(r))
+    o["final_residual"] = r.option(lambda: _f32_vec(r))
+    o["logits_i32"] = r.option(lambda: _i32_vec(r))
+    o["lp_hidden_bf16"] = r.option(lambda: r.vec(lambda: struct.unpack("<H", r.take(2))[0]))
+    o["captured_logits_f32"] = r.option(lambda: _f32_vec(r))
+    return o
+
+
+def read_v4_audit_rest(r: Bincode, out: dict) -> None:
+    """The fields of V4AuditResponse after revealed_seed (types.rs:1502-1567)."""
+    out["shell_opening"] = r.option(lambda: read_shell_opening(r))
+    out["manifest"] = r.option(lambda: read_manifest(r))
+    out["prompt_field"] = r.option(lambda: r.bytes_vec().hex())
+    out["n_prompt_tokens"] = r.option(r.u32)
+    out["output_text"] = r.option(lambda: r.bytes_vec().decode())
+    out["prefix_embedding_rows"] = r.option(lambda: r.vec(lambda: _f32_vec(r)))
+    out["prefix_embedding_proofs"] = r.option(lambda: r.vec(lambda: read_proof(r)))
+    if r.u8() != 0:
+        raise ValueError("prefix_retained present: not decoded here")
+    if r.u8() != 0:
+        raise ValueError("prefix_shell_openings present: not decoded here")
+    out["prefix_retained"] = out["prefix_shell_openings"] = None
+    out["kv_entries"] = r.option(lambda: r.vec(lambda: r.vec(lambda: {"k_roped": r.bytes_vec_f64(),
+                                                                     "v_deq": r.bytes_vec_f64()})))
+    out["kv_proofs"] = r.option(lambda: r.vec(lambda: r.vec(lambda: read_proof(r))))
+    out["witnessed_scores"] = r.option(lambda: r.vec(lambda: {"scores": _f32_vec(r), "n_q_heads": r.u64(),
+                                                              "seq_len": r.u64()}))
+    if r.o != len(r.b):
+        raise ValueError(f"{len(r.b) - r.o} bytes left after witnessed_scores")
+
+
+def _rust_value(text: str):
+    """A value of golden_manifest()'s struct literal as the Python value the
+    manifest dicts use: [u8; 32] as hex, Option as None, strings, numbers."""
+    t = text.strip()
+    if t == "None":
+        return None
+    if t.startswith("Some(") and t.endswith(")"):
+        return _rust_value(t[5:-1])
+    m = re.fullmatch(r"\[(0x[0-9a-fA-F]+|\d+)u?8?; 32\]", t)
+    if m:
+        return bytes([int(m.group(1), 0)] * 32).hex()
+    if t in ("vec![]",):
+        return []
+    if t == "String::new()":
+        return ""
+    m = re.fullmatch(r'"(.*)"\.into\(\)', t)
+    if m:
+        return m.group(1)
+    if t in ("true", "false"):
+        return t == "true"
+    if re.fullmatch(r"-?\d+", t):
+        return int(t)
+    return float(t)
+
+
+def golden_manifest(ref_root: str):
+    src = open(os.path.join(ref_root, "crates/verilm-test-vectors/tests/golden_conformance.rs")).read()
+    body = re.search(r"fn golden_manifest\(\) -> DeploymentManifest \{\s*DeploymentManifest \{(.*?)\n    \}\n\}",
+                     src, flags=re.S).group(1)
+    m = {}
+    for line in body.splitlines():
+        line = line.strip().rstrip(",")
+        if not line or line.startswith("//"):
+            continue
+        k, v = line.split(":", 1)
+        m[k.strip()] = _rust_value(v)
+    pins = {}
+    for test, key in (("golden_manifest_hash", "manifest_hash"), ("golden_model_spec_hash", "model_spec_hash")):
+        blk = re.search(r"fn " + test + r"\(\) \{(.*?)\n\}", src, flags=re.S).group(1)
+        pins[key] = re.search(r'"([0-9a-f]{64})"', blk).group(1)
+    return {"manifest": m, **pins, "source": "golden_conformance.rs:132-201"}
 
 
 def main(ref_root: str) -> None:
@@ -155,6 +320,15 @@ def main(ref_root: str) -> None:
         if pin is not None and file_sha != pin:
             raise SystemExit(f"{name}: file checksum {file_sha} != cross_version.rs pin {pin}")
         rec = read_v4_audit_prefix(blob)
+        r = Bincode(zstd_decompress(blob[4:]))
+        full = read_v4_audit_prefix(blob)
+        r.o = _prefix_len(blob)
+        read_v4_audit_rest(r, full)
+        for k in ("shell_opening", "manifest", "prompt_field", "n_prompt_tokens", "output_text",
+                  "prefix_embedding_rows", "prefix_embedding_proofs", "prefix_retained", "prefix_shell_openings",
+                  "kv_entries", "kv_proofs", "witnessed_scores"):
+            rec[k] = full[k]
+        rec["bincode_hex"] = r.b.hex()
         rec["file_sha256"] = file_sha
         rec["prompt"] = prompt          # gen_fixtures.rs:313, 389
         rec["sampling_seed"] = "07" * 32  # gen_fixtures.rs:314, 390
@@ -169,10 +343,13 @@ def main(ref_root: str) -> None:
         "merkle_root": "de54562ec98e6ec3dc1cb484758553713dc93caffee16d167cd2064dd512a880",
         "io_root": "62240adf4325d2c15b3d81be456351851d4796d6ba202fd7e24fc4c5729cf5f7",
     }
+    pins["golden_manifest"] = golden_manifest(ref_root)
     with open(os.path.join(HERE, "reference_pins.json"), "w") as f:
         json.dump(pins, f, indent=1, sort_keys=True)
     print("wrote", os.path.join(HERE, "reference_pins.json"))
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -24,7 +24,7 @@ def test_reference_arm_default_workload():
     assert d["value"] > 0 and d["unit"] == "GB/s" and d["higher_is_better"] is True
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert d["config"]["workload"] == "llama3.1-8b-kv"
+    assert d["config"]["workload"] == "llama3.1-70b-kv-32x32768" and d["scaling"] == "strong"
 
 
 def test_reference_arm_online_is_unavailable():

@@ -44,7 +44,7 @@ def test_uniform_shard_plans_are_row_major():
             assert D.tree_order(plan, L) == [(s, l) for s in range(S) for l in range(L)]
 
 
-def _worker(rank, world, port, S, L, fail_rank, q):
+def _worker(rank, world, port, S, L, fail_rank, q, plan=None):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         import datetime
@@ -53,7 +53,7 @@ def _worker(rank, world, port, S, L, fail_rank, q):
         import torch.distributed as dist
         from tests import kvref
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
-        plan = D.shard_plan(S, L, world)
+        plan = plan or D.shard_plan(S, L, world)
         sh = plan[rank]
         tr = kvref.contiguous(55, L, [9 + 3 * s for s in range(S)], 2, 8)
         if rank == fail_rank:
@@ -70,11 +70,11 @@ def _worker(rank, world, port, S, L, fail_rank, q):
         q.put((rank, "err", f"{type(e).__name__}: {e}", traceback.format_exc(), None))
 
 
-def _run(world, S, L, fail_rank=-1, timeout=120):
+def _run(world, S, L, fail_rank=-1, timeout=120, plan=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, S, L, fail_rank, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, S, L, fail_rank, q, plan)) for r in range(world)]
     for p in ps:
         p.start()
     out = []
@@ -95,6 +95,20 @@ def test_gather_roots_reassembles_single_process_roots(world, S, L):
     for r in res:
         assert r[2] == want              # every rank holds every kv_root, in order
         assert r[3] == res[0][3]         # and the same root-of-roots
+
+
+def test_gather_roots_equal_shards_in_another_order():
+    """A caller's plan with equal shards that do not tile the grid row-major
+    (2 sequences x 4 ranks, each sequence's layers in halves, sequences
+    interleaved) must still come back in (sequence, layer) order."""
+    S, L = 2, 4
+    plan = [D.Shard(0, 1, 0, 2), D.Shard(1, 2, 0, 2), D.Shard(0, 1, 2, 4), D.Shard(1, 2, 2, 4)]
+    assert D.tree_order(plan, L) != [(s, l) for s in range(S) for l in range(L)]
+    res = _run(4, S, L, plan=plan)
+    assert all(r[1] == "ok" for r in res), res
+    for r in res:
+        assert r[2] == res[0][4]
+        assert r[3] == res[0][3]
 
 
 def test_failed_rank_does_not_hang_the_others():

@@ -77,3 +77,35 @@ def test_noalloc_rejects_sizes_beyond_its_maximum():
     st = _lib.lib().vc_kv_commit_noalloc(ctypes.byref(d), ctypes.c_void_p(roots.data_ptr()), None, None)
     assert st == _lib.VC_EINVAL
     assert "bytes of scratch" in _lib.last_error()
+
+
+def test_noalloc_flags_bad_page_ids(ctx):
+    """A block table holding -1 and a page past the cache: the kernel checks
+    each page id before it reads the page, skips the row and sets the flag,
+    so the caller learns that the roots of this call are void."""
+    stream = torch.cuda.current_stream(ctx.device)
+    tr = kvref.paged(506, 2, [40, 33], 2, 64, block_size=16)
+    n_pages = tr.k.shape[1]
+    bt = tr.block_tables.copy()
+    bt[0, 1] = -1
+    bt[1, 0] = n_pages + 5
+    tr.block_tables = bt
+    view = tr.view(ctx.device)
+    _, flag = _noalloc(view, stream)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 1
+    # the same table through the allocating entry point reports VC_ERANGE
+    C.kv_commit(ctx, view, keep_trees=False)
+    with pytest.raises(_lib.VcValueError):
+        ctx.sync(timeout_ms=60000)
+
+
+def test_noalloc_refuses_paged_layout_without_flag():
+    tr = kvref.paged(507, 1, [20], 2, 64, block_size=16)
+    view = tr.view(0)
+    d, keep = C._kv_desc(view)
+    roots = torch.zeros(1, 1, 32, dtype=torch.uint8, device="cuda:0")
+    st = _lib.lib().vc_kv_commit_noalloc(ctypes.byref(d), ctypes.c_void_p(roots.data_ptr()), None, None)
+    assert st == _lib.VC_EINVAL
+    assert "err_flag_dev" in _lib.last_error()
+    del keep

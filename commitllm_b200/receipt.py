@@ -305,7 +305,7 @@ def _json_f32(x: float):
     x = np.float32(x)
     if not np.isfinite(x):
         return None                       # serde_json writes non-finite floats as null
-    return float(repr(x)) if repr(x) != "-0.0" else -0.0
+    return float(str(x))                  # the shortest decimal that reads back as this f32
 
 
 def _to_json(t: T, v: Any):

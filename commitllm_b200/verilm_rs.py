@@ -17,13 +17,21 @@ either, as in the reference, from ``compute_kv_transcript`` when both
 committing the same leaf encoding ``hash_kv_entry`` (merkle.rs:285-293) over
 the cache's values widened to f64.
 
-Not provided here (outside the commitment hot path): the deployment-manifest
-hash (``manifest=`` raises NotImplementedError), loading weights from a
-safetensors directory, and ``audit_v4``'s shell opening.  Openings of the
-committed trees are available as ``*_proof`` methods.
+``manifest=`` binds the deployment manifest exactly as the reference does
+(four-spec hashes composed into ``manifest_hash``, prover/src/lib.rs:422-440),
+hashed on the host once per request (:mod:`commitllm_b200.manifest`).
+``audit_v4`` / ``audit_v4_binary`` return the reference's ``V4AuditResponse``
+(JSON, or ``"VV4A" || zstd(bincode)``) built from the GPU trees: retained
+state, retained / IO / prefix proofs and the KV entries with their proofs,
+as ``open_v4_structural`` plus the KV part of ``open_v4`` build them
+(prover/src/lib.rs:1564-1687).  Not provided (outside the commitment path):
+the shell opening, whose matrix-product replay from the model weights is
+verifier-side math (``shell_opening`` is ``None``), and loading weights from a
+safetensors directory.
 """
 from __future__ import annotations
 
+import ctypes
 import json
 import struct
 from typing import List, Optional, Sequence
@@ -32,6 +40,9 @@ import numpy as np
 import torch
 
 from . import commit as C
+from . import manifest as _manifest
+from . import receipt as _receipt
+from ._lib import check, lib
 
 # MatrixType::PER_LAYER order (crates/verilm-core/src/constants.rs:26-34)
 MATRIX_TYPES = ("Wq", "Wk", "Wv", "Wo", "Wg", "Wu", "Wd")
@@ -204,8 +215,13 @@ class _Committed:
     """Device results of one request's commit; host copies made on first use."""
 
     def __init__(self, ctx, n_tokens, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees,
-                 n_kv_layers):
+                 n_kv_layers, manifest=None, prompt=b"", seed=bytes(32), layout=None):
         self._ctx = ctx
+        self._manifest = manifest        # DeploymentManifest (manifest.from_dict) or None
+        self._spec = _manifest.spec_hashes(manifest) if manifest is not None else None
+        self._prompt = bytes(prompt)
+        self._seed = bytes(seed)
+        self._layout = layout            # where each token's retained rows live on the device
         self._n_tokens = n_tokens
         self._token_ids = list(token_ids)
         self._n_prompt_tokens = n_prompt_tokens
@@ -227,15 +243,24 @@ class _Committed:
         return self._host
 
     # --- reference handle API (verilm-py/src/lib.rs:651-674) ---
-    def commitment(self) -> dict:
+    def _batch_commitment(self) -> dict:
+        """``BatchCommitment`` (types.rs:1710-1759) with [u8; 32] fields as bytes."""
         h = self._h()
+        sp = self._spec or {}
         return {
-            "merkle_root": list(h["merkle_root"]), "io_root": list(h["io_root"]), "n_tokens": self._n_tokens,
-            "manifest_hash": None, "input_spec_hash": None, "model_spec_hash": None,
-            "decode_spec_hash": None, "output_spec_hash": None, "version": "V4",
-            "prompt_hash": list(h["prompt_hash"]), "seed_commitment": list(h["seed_commitment"]),
-            "n_prompt_tokens": self._n_prompt_tokens, "kv_roots": [list(r) for r in h["kv_roots"]],
+            "merkle_root": h["merkle_root"], "io_root": h["io_root"], "n_tokens": self._n_tokens,
+            "manifest_hash": sp.get("manifest_hash"), "input_spec_hash": sp.get("input_spec_hash"),
+            "model_spec_hash": sp.get("model_spec_hash"), "decode_spec_hash": sp.get("decode_spec_hash"),
+            "output_spec_hash": sp.get("output_spec_hash"), "version": "V4",
+            "prompt_hash": h["prompt_hash"], "seed_commitment": h["seed_commitment"],
+            "n_prompt_tokens": self._n_prompt_tokens, "kv_roots": list(h["kv_roots"]),
         }
+
+    def commitment(self) -> dict:
+        """The serde_json value of ``BatchCommitment``: digests as lists of byte values."""
+        c = self._batch_commitment()
+        return {k: (list(v) if isinstance(v, bytes) else ([list(x) for x in v] if k == "kv_roots" else v))
+                for k, v in c.items()}
 
     def commitment_json(self) -> str:
         """serde_json form of ``BatchCommitment`` (types.rs:1710-1759)."""
@@ -248,7 +273,7 @@ class _Committed:
         return self._h()["io_root"].hex()
 
     def manifest_hash_hex(self):
-        return None
+        return self._spec["manifest_hash"].hex() if self._spec else None
 
     def n_tokens(self) -> int:
         return self._n_tokens
@@ -328,20 +353,82 @@ class _Committed:
                 out += struct.pack("<IQ", p, layer.shape[1]) + layer[p].tobytes()
         return bytes(out)
 
+    # --- audit receipts (verilm-py/src/lib.rs:681-786) ---
+    def _retained(self, t: int) -> dict:
+        """``RetainedTokenState`` of token t (types.rs:1201-1229), read back from the
+        capture rows its leaf hashed; x_attn is None, as build_retained_from_captures
+        leaves it (prover/src/lib.rs:162-167)."""
+        lay = self._layout
+        f, row = int(lay.tok_fwd[t]), int(lay.tok_row[t])
+        dev = f"cuda:{self._ctx.device}"
+        layers = []
+        for l in range(lay.n_layers):
+            a = torch.as_tensor(C._DevView(int(lay.a_rows[f][l]) + row * lay.hidden, lay.hidden, self), device=dev)
+            sc = torch.as_tensor(C._DevView(int(lay.scale_a[f][l]) + 4 * row * lay.scale_stride, 4, self), device=dev)
+            layers.append({"a": bytes(a.cpu().numpy()), "scale_a": struct.unpack("<f", bytes(sc.cpu().numpy()))[0],
+                           "x_attn_i8": None, "scale_x_attn": None})
+        return {"layers": layers}
+
+    def _proofs(self, trees: C.TreeSet, tree: int, leaves: Sequence[int]) -> list:
+        if not leaves:
+            return []
+        sib, depth = trees.prove([tree] * len(leaves), list(leaves))
+        s = sib.cpu().numpy()
+        return [{"leaf_index": int(j), "siblings": [bytes(x) for x in s[k, :depth[k]]]} for k, j in enumerate(leaves)]
+
+    def v4_audit_response(self, token_index: int, layer_indices=None, output_text=None,
+                          include_kv: bool = True) -> dict:
+        """The ``V4AuditResponse`` (types.rs:1475-1567) of one challenged token as
+        open_v4_structural builds it (prover/src/lib.rs:1596-1687), plus the KV
+        entries and proofs of open_v4 (1564-1588) for ``layer_indices`` (all
+        committed layers when None).  ``shell_opening`` is None: the shell replay
+        is verifier-side math this library does not build."""
+        i = int(token_index)
+        if not 0 <= i < self._n_tokens:
+            raise ValueError(f"token_index {token_index} out of range (n_tokens={self._n_tokens})")
+        if self._layout is None:
+            raise ValueError("this handle keeps no capture layout to open")
+        leaves = self._trees.nodes(0)[: self._n_tokens].cpu().numpy()
+        ios = self._trees.nodes(1)[: self._n_tokens].cpu().numpy()
+        if i == 0:
+            ph = self._ctx.to_device(np.frombuffer(self._h()["prompt_hash"], np.uint8).reshape(1, 32))
+            g = self._ctx.empty(1, 32)
+            check(lib().vc_io_genesis(self._ctx.handle, 1, ctypes.c_void_p(ph.data_ptr()),
+                                      ctypes.c_void_p(g.data_ptr())))
+            prev = bytes(g.cpu().numpy()[0])
+        else:
+            prev = bytes(ios[i - 1])
+        resp = {
+            "token_index": i, "retained": self._retained(i),
+            "merkle_proof": self._proofs(self._trees, 0, [i])[0], "io_proof": self._proofs(self._trees, 1, [i])[0],
+            "token_id": int(self._token_ids[i]) & 0xFFFFFFFF, "prev_io_hash": prev,
+            "prefix_leaf_hashes": [bytes(x) for x in leaves[:i]],
+            "prefix_merkle_proofs": self._proofs(self._trees, 0, list(range(i))),
+            "prefix_token_ids": np.asarray([int(x) & 0xFFFFFFFF for x in self._token_ids[:i]], dtype="<u4"),
+            "commitment": self._batch_commitment(), "revealed_seed": self._seed, "shell_opening": None,
+            "manifest": self._manifest, "prompt": self._prompt, "n_prompt_tokens": self._n_prompt_tokens,
+            "output_text": output_text, "prefix_embedding_rows": None, "prefix_embedding_proofs": None,
+            "prefix_retained": None, "prefix_shell_openings": None, "kv_entries": None, "kv_proofs": None,
+            "witnessed_scores": None,
+        }
+        if include_kv and self._kv_trees is not None:
+            layers, ent, sib = self.kv_openings(i, layer_indices)
+            resp["kv_entries"] = [[{"k_roped": e[0].astype("<f8"), "v_deq": e[1].astype("<f8")} for e in lay]
+                                  for lay in ent]
+            resp["kv_proofs"] = [[{"leaf_index": p, "siblings": [bytes(x) for x in lay[p]]}
+                                  for p in range(lay.shape[0])] for lay in sib]
+        return resp
+
     def audit_v4(self, token_index: int, layer_indices=None, output_text=None, include_kv: bool = True) -> str:
-        """``audit_v4`` (verilm-py/src/lib.rs:681-712) builds a whole ``V4AuditResponse``,
-        whose shell openings replay the model's matrix products from the weights on
-        the CPU: verifier-side math outside this commitment library.  Its commitment
-        parts are here: ``retained_proof`` / ``io_proof`` and, for the KV fields,
-        ``audit_kv_json`` / ``audit_kv_bincode``."""
-        raise NotImplementedError("audit_v4 needs the shell openings (weight replay), which this GPU commit "
-                                  "library does not build; use retained_proof, io_proof and audit_kv_json")
+        """serde_json of the token's ``V4AuditResponse`` (verilm-py/src/lib.rs:683-695)."""
+        return _receipt.v4_audit_json(self.v4_audit_response(token_index, layer_indices, output_text, include_kv))
 
     def audit_v4_binary(self, token_index: int, layer_indices=None, output_text=None,
                         include_kv: bool = True) -> bytes:
-        """See :meth:`audit_v4`; the binary form would be ``VV4A`` || zstd(bincode)."""
-        raise NotImplementedError("audit_v4_binary needs the shell openings (weight replay), which this GPU "
-                                  "commit library does not build; use audit_kv_bincode for the KV fields")
+        """``"VV4A" || zstd(bincode)`` of the token's ``V4AuditResponse``
+        (verilm-py/src/lib.rs:699-712, serialize.rs:43-50)."""
+        return _receipt.serialize_v4_audit(self.v4_audit_response(token_index, layer_indices, output_text,
+                                                                   include_kv))
 
     def leaf_hashes(self) -> torch.Tensor:
         """The retained leaves (tree 0's level 0), a device view ``[n_tokens, 32]``."""
@@ -370,18 +457,19 @@ class PackedBatchStateHandle(_Committed):
 
 
 def _check_common(token_ids, sampling_seed, manifest):
-    if manifest is not None:
-        raise NotImplementedError("manifest hashing is not part of the GPU commit path; pass manifest=None")
+    """Argument checks of the boundary (verilm-py/src/lib.rs:843-897); returns
+    the seed and the parsed manifest (extract_manifest, lib.rs:173-490) or None."""
     seed = bytes(sampling_seed)
     if len(seed) != 32:
         raise ValueError("sampling_seed must be exactly 32 bytes")
     for t in token_ids:
         if not 0 <= int(t) <= 0xFFFFFFFF:
             raise ValueError(f"token id {t} does not fit u32")
-    return seed
+    return seed, (_manifest.from_dict(manifest) if manifest is not None else None)
 
 
-def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens, kv_cache, handle_cls, **extra):
+def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens, kv_cache, handle_cls,
+            manifest=None, **extra):
     n = len(layout.tok_fwd)
     if n != len(token_ids):
         raise ValueError("retained state count must match token_ids")
@@ -406,7 +494,8 @@ def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens
         r, kv_trees = C.kv_commit(ctx, kv_cache, keep_trees=True)
         kv_roots = r[0]
         n_kv_layers = len(kv_cache.k_layers)
-    h = handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers, **extra)
+    h = handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers,
+                   manifest=manifest, prompt=prompt, seed=seed, layout=layout, **extra)
     h._kv_view = kv_cache
     return h
 
@@ -426,7 +515,7 @@ def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_size
                                  ctx: Optional[C.Context] = None) -> MinimalBatchStateHandle:
     """V4 commitment from minimal captures (verilm-py/src/lib.rs:800-985)."""
     ctx = ctx or C.Context()
-    seed = _check_common(token_ids, sampling_seed, manifest)
+    seed, man = _check_common(token_ids, sampling_seed, manifest)
     fwd_batch_sizes = [int(b) for b in fwd_batch_sizes]
     n_layers = int(n_layers)
     scales_h = scales if (isinstance(scales, torch.Tensor) and scales.is_cuda) else _f32_host(scales)
@@ -494,7 +583,7 @@ def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_size
         kv_cache = C.kv_transcript_view(k, v)
         keep += [k, v] + held
     h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle,
-                x_attn=x_attn_inputs)
+                manifest=man, x_attn=x_attn_inputs)
     h._inputs = keep
     return h
 
@@ -505,7 +594,7 @@ def commit_minimal_packed(packed_a, packed_scales, n_layers, hidden_dim, fwd_bat
                           ctx: Optional[C.Context] = None) -> PackedBatchStateHandle:
     """V4 commitment from packed buffers (verilm-py/src/lib.rs:1189-1310)."""
     ctx = ctx or C.Context()
-    seed = _check_common(token_ids, sampling_seed, manifest)
+    seed, man = _check_common(token_ids, sampling_seed, manifest)
     fwd_batch_sizes = [int(b) for b in fwd_batch_sizes]
     n_layers, hidden_dim = int(n_layers), int(hidden_dim)
     n_tok = sum(fwd_batch_sizes)
@@ -549,6 +638,6 @@ def commit_minimal_packed(packed_a, packed_scales, n_layers, hidden_dim, fwd_bat
         lay.final_residual = fr.view(torch.float32).view(n_tok, int(final_res_dim))
         lay.tok_fr_row = list(range(n_tok))
         keep.append(fr)
-    h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, PackedBatchStateHandle)
+    h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, PackedBatchStateHandle, manifest=man)
     h._inputs = keep
     return h

@@ -62,6 +62,10 @@ WORKLOADS = {
                    vocab=128256, x_attn=True, steps=6),
     "c2t": dict(kind="kvt", name="llama3.1-8b-kv-transcript", n_layers=32, n_heads=8, head_dim=128, hidden=4096,
                 n_seqs=1, seq_len=4096, rope="llama3", steps=250),
+    # one whole request through verilm_rs.commit_request: Llama-3.1-8B shapes, 1024 prompt tokens + 3 072
+    # decode steps (4 096 committed tokens), captured logits for the 3 073 generated tokens, its KV cache
+    "request": dict(kind="request", name="llama3.1-8b-request-4096", n_layers=32, hidden=4096, n_heads=8,
+                    head_dim=128, n_seqs=1, seq_len=4096, n_prompt=1024, vocab=128256, x_attn=False, steps=20),
 }
 
 
@@ -97,6 +101,16 @@ def algorithmic(w):
         leaves = w["n_seqs"] * w["seq_len"] * w["n_layers"]
         blocks = leaves * sha_blocks(16 + 16 * kv) + w["n_seqs"] * w["n_layers"] * tree_blocks(w["seq_len"])
         return blocks, 0, leaves * kv * 4, leaves * (16 + 16 * kv), w["n_seqs"] * w["n_layers"]
+    if w["kind"] == "request":
+        L, H, V, n = w["n_layers"], w["hidden"], w["vocab"], w["seq_len"]
+        kv = w["n_heads"] * w["head_dim"]
+        n_gen = n - (w["n_prompt"] - 1)
+        base = 14 + L * (H + 4 + 1)
+        trace = n * sha_blocks(base) + n_gen * sha_blocks(21 + 32 + 4 * V)
+        kv_blocks = n * L * sha_blocks(16 + 16 * kv) + L * tree_blocks(n)
+        other = 2 * n + 2 * tree_blocks(n) + kv_blocks
+        src = n * L * (H + 4) + n_gen * 4 * V + n * L * kv * 4
+        return trace, other, src, n * base + n_gen * (21 + 32 + 4 * V) + n * L * (16 + 16 * kv), 2 + L
     L, H, V = w["n_layers"], w["hidden"], w["vocab"]
     per_layer = H + 4 + 1 + ((H + 4) if w["x_attn"] else 0)
     base = 14 + L * per_layer
@@ -531,6 +545,80 @@ class TraceStep:
 
 
 # ---------------------------------------------------------------------------
+# Whole-request workload
+# ---------------------------------------------------------------------------
+
+REQUEST_MANIFEST = {"tokenizer_hash": "11" * 32, "temperature": 0.7, "top_k": 50, "top_p": 0.9, "eos_policy": "stop",
+                    "weight_hash": "22" * 32, "quant_hash": "33" * 32, "system_prompt_hash": "44" * 32,
+                    "max_tokens": 3072, "sampler_version": "chacha20-vi-sample-v1", "decode_mode": "sampled",
+                    "n_layers": 32, "hidden_dim": 4096, "vocab_size": 128256, "kv_dim": 1024, "d_head": 128,
+                    "n_q_heads": 32, "n_kv_heads": 8, "rope_theta": 500000.0, "rmsnorm_eps": 1e-5}
+
+
+class RequestStep:
+    """One request's whole commitment through ``verilm_rs.commit_request`` (captures
+    and KV cache resident), ending with the commitment read back to the host, as a
+    server returns it.  The timed interval is the request's latency on the GPU
+    timeline, host orchestration included."""
+
+    def __init__(self, w, ctx, stream, device, rank, world):
+        import torch
+        from commitllm_b200 import commit as C
+        from commitllm_b200 import verilm_rs as V
+        self.C, self.V, self.torch = C, V, torch
+        self.w, self.ctx, self.stream, self.world = w, ctx, stream, world
+        dev = f"cuda:{device}"
+        g = torch.Generator(device=dev)
+        g.manual_seed(6000 + rank)
+        L, H, n, Vb = w["n_layers"], w["hidden"], w["seq_len"], w["vocab"]
+        self.n_gen = n - (w["n_prompt"] - 1)
+        self.a = torch.randint(-128, 128, (n, L, H), generator=g, device=dev, dtype=torch.int8)
+        self.sa = torch.rand(n, L, generator=g, device=dev) * 0.05 + 1e-3
+        self.logits = torch.randn(self.n_gen, Vb, generator=g, device=dev) * 3.0
+        self.tok = torch.randint(0, Vb, (n,), generator=g, device=dev, dtype=torch.int32)
+        self.view = make_view(dict(w, paged=False), device, seed=7000 + rank)
+        self.kernel_events = []
+        self.launches = 6     # trace leaves, prompt hash, IO chain, trace/IO trees, seed commitment, KV trees
+
+    def commit(self, ctx=None):
+        return self.V.commit_request(self.a, self.sa, self.tok, b"synthetic prompt", b"\x07" * 32,
+                                     n_prompt_tokens=self.w["n_prompt"], captured_logits_f32=self.logits,
+                                     kv_cache=self.view, manifest=REQUEST_MANIFEST, ctx=ctx or self.ctx)
+
+    def __call__(self, timed: bool):
+        torch = self.torch
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        h = self.commit()
+        self.last = h.commitment_json()        # synchronises: the roots are on the host
+        e1.record(self.stream)
+        if timed:
+            self.kernel_events.append((e0, e1))
+
+    def phases(self):
+        """Device time of each part on its own (ms): trace leaves, IO chain, KV trees."""
+        torch, C = self.torch, self.C
+        n = self.w["seq_len"]
+        h = self.commit()
+        lay = h._layout
+        leaves = self.ctx.empty(n, 32)
+        ph = C.prompt_hashes(self.ctx, [b"synthetic prompt"])
+        io = self.ctx.empty(n, 32)
+        out = {}
+        for name, fn in (("trace_leaves", lambda: C.trace_leaves(self.ctx, lay, out=leaves)),
+                         ("io_chain", lambda: C.io_chain(self.ctx, leaves, self.tok, ph, [0, n], out=io)),
+                         ("kv_trees", lambda: C.kv_commit(self.ctx, self.view, keep_trees=True)[1].free())):
+            fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(self.stream)
+            fn()
+            b.record(self.stream)
+            torch.cuda.synchronize()
+            out[name] = round(a.elapsed_time(b), 3)
+        return out
+
+
+# ---------------------------------------------------------------------------
 # CPU legs: the oracle's C restatement of the reference algorithm
 # ---------------------------------------------------------------------------
 
@@ -562,8 +650,8 @@ def cpu_kv(w, n_layers, n_threads, reps=1, seed=7):
     return sorted(ts)[len(ts) // 2]
 
 
-def cpu_trace(w, n_tokens, n_threads, reps=1, seed=9):
-    """Seconds to hash n_tokens retained leaves (+ their IO chain) of the c4 workload on the host."""
+def cpu_trace(w, n_tokens, n_threads, reps=1, seed=9, logits_wrap=True):
+    """Seconds to hash n_tokens retained leaves (+ their IO chain) of the c4 / request workload on the host."""
     import ctypes
     import numpy as np
     from commitllm_b200._lib import TraceDesc
@@ -596,8 +684,9 @@ def cpu_trace(w, n_tokens, n_threads, reps=1, seed=9):
         d.x_attn_rows = per_layer(x, n_tokens * H)
         d.scale_x_attn = per_layer(sc, n_tokens * 4)
         d.scale_x_stride = 1
-    d.logits, d.vocab, d.logits_rows, d.logits_stride = logits.ctypes.data, V, n_tokens, V
-    d.tok_logits_row = i32(list(range(n_tokens)))
+    if logits_wrap:
+        d.logits, d.vocab, d.logits_rows, d.logits_stride = logits.ctypes.data, V, n_tokens, V
+        d.tok_logits_row = i32(list(range(n_tokens)))
     leaves = np.zeros((n_tokens, 32), np.uint8)
     toks = rng.integers(0, V, size=n_tokens, dtype=np.uint32)
     ts = []
@@ -654,6 +743,25 @@ def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
                   f"{threads} thread(s)) + KV trees of {layers} of {w['n_layers']} layers ({dt_h:.2f} s, "
                   f"{kv_threads} thread(s)), oracle C restatement, extrapolated linearly to the workload")
         return src_full / total / 1e9, threads, sample, total
+    if w["kind"] == "request":
+        # commit_minimal as the reference runs it (prover/src/lib.rs:336-544): trace leaves on all host
+        # threads (rayon, 371-393), the IO chain serial (403-410), the KV trees in a sequential
+        # per-layer loop (454-478); each part timed on a sample and scaled to the request
+        n = w["seq_len"]
+        n_gen = n - (w["n_prompt"] - 1)
+        threads = ncpu
+        n_tok = max(64, 8 * threads)
+        dt_l = cpu_trace(w, n_tok, threads, logits_wrap=True) / n_tok
+        dt_b = cpu_trace(w, n_tok, threads, logits_wrap=False) / n_tok
+        kv_threads = 1 if reference_threads else max(1, min(ncpu, w["n_layers"]))
+        wkv = dict(w, kind="kv", paged=False)
+        layers = max(1, min(w["n_layers"], kv_threads, 8))
+        dt_kv = cpu_kv(wkv, layers, kv_threads) / layers * w["n_layers"]
+        total = dt_l * n_gen + dt_b * (n - n_gen) + dt_kv
+        sample = (f"{n_tok} tokens with and {n_tok} without the logits wrap ({threads} threads, IO chain serial) + "
+                  f"{layers} of {w['n_layers']} KV trees ({kv_threads} thread(s)), oracle C restatement, scaled to "
+                  f"{n_gen} + {n - n_gen} tokens and {w['n_layers']} trees; KV part {dt_kv:.2f} s")
+        return src_full / total / 1e9, threads, sample, total
     if w["kind"] == "kv":
         # the reference hashes KV trees in a sequential per-layer loop (prover/src/lib.rs:454-478);
         # every (sequence, layer) tree costs the same, so the sample is whole trees of one
@@ -698,7 +806,7 @@ def run_online(args, w, local):
     stream = torch.cuda.Stream(local)
     ctx = C.Context(local, stream)
     n_steps = args.steps + args.warmup
-    oc = OnlineCommitter(ctx, max_slots=B, max_tokens=2 * n_steps + 4)
+    oc = OnlineCommitter(ctx, max_slots=B, max_tokens=2 * n_steps + 4, defer_tokens=0)
     for s_ in range(B):
         oc.open(s_, b"synthetic prompt %d" % s_, bytes([s_ % 256]) * 32, n_prompt_tokens=1)
     g = torch.Generator(device=dev)
@@ -896,6 +1004,11 @@ def main():
         args.no_e2e = True
     elif w.get("job"):
         step = KvJobStep(w, ctx, stream, local, rank, world)
+    elif w["kind"] == "request":
+        if world > 1:
+            raise SystemExit("the request workload runs on one GPU")
+        step = RequestStep(w, ctx, stream, local, rank, world)
+        args.no_e2e = True
     else:
         step = {"kv": KvStep, "kvt": KvtStep, "trace": TraceStep}[w["kind"]](w, ctx, stream, local, rank, world)
     torch.cuda.synchronize()
@@ -1021,6 +1134,8 @@ def main():
                     "what": "merkle::prove of random (sequence, layer, position) leaves, batched, device"}
         del sib
         trees_o.free()
+
+    request_phases = step.phases() if w["kind"] == "request" else None
 
     # integer-ALU peak probe on the same GPU, same run
     peak_ops = C.int_peak(ctx, 0, 4000)
@@ -1175,6 +1290,20 @@ def main():
         "gpu_launches": args.steps * step.launches,
         "clocks": clocks,
     }
+    if w["kind"] == "request":
+        ops = (blocks + other_blocks) * BLK_OPS / (ms_step * 1e-3) / 1e12
+        line["roofline"] = {
+            "bound": "latency", "achieved": round(ops, 3), "peak": round(alu_peak, 3), "unit": "Tops/s",
+            "frac": round(ops / alu_peak, 4), "traffic": None, "algorithmic_bytes": src_bytes,
+            "kernel": "commit_request (trace_leaf_kernel, io_chain_kernel, tree_commit_kernel, kv_commit_kernel)",
+            "note": "one request: %d serial SHA chains for the trace leaves (%d blocks each with the logits "
+                    "wrap), then the IO chain, 2 dependent blocks per token; the KV trees run on a second stream "
+                    "beside them" % (w["seq_len"], sha_blocks(14 + w["n_layers"] * (w["hidden"] + 5))
+                                     + sha_blocks(53 + 4 * w["vocab"]))}
+        ph = request_phases
+        line["phases_ms"] = ph
+        line["io_chain_share"] = round(ph["io_chain"] / ms_step, 3)
+        line["serial_floor_ms"] = round(ph["trace_leaves"] + ph["io_chain"], 3)
     if w["kind"] in ("kv", "kvt"):
         line["kv_roots_per_s"] = line["roots_per_s"]
     if w["kind"] == "kvt":

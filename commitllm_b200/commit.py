@@ -70,7 +70,25 @@ class Context:
         self.device = torch.cuda.current_device() if device is None else int(device)
         self.stream = stream if stream is not None else torch.cuda.current_stream(self.device)
         self._h = ctypes.c_void_p()
+        self._side = None
         check(lib().vc_ctx_create(self.device, ctypes.c_void_p(self.stream.cuda_stream), ctypes.byref(self._h)))
+
+    def side(self) -> "Context":
+        """A second context of this device on its own stream, for work that
+        should overlap this context's (created on first use, then kept)."""
+        if self._side is None:
+            self._side = Context(self.device, torch.cuda.Stream(self.device))
+        return self._side
+
+    def fork(self) -> "Context":
+        """The side context, ordered after everything queued on this one so far."""
+        s = self.side()
+        s.stream.wait_stream(self.stream)
+        return s
+
+    def join(self, other: "Context") -> None:
+        """Order this context's later work after everything queued on ``other``."""
+        self.stream.wait_stream(other.stream)
 
     @property
     def handle(self) -> ctypes.c_void_p:
@@ -82,6 +100,9 @@ class Context:
         check(lib().vc_ctx_sync(self.handle, int(timeout_ms)))
 
     def close(self) -> None:
+        if self._side is not None:
+            self._side.close()
+            self._side = None
         if self._h:
             lib().vc_ctx_destroy(self._h)
             self._h = ctypes.c_void_p()

@@ -13,10 +13,16 @@ SHA-256 is serial within a message, so one pass of B tokens is B independent
 chains: a decode step of 256 long leaves (logits wraps of 8 017 blocks) is
 latency-bound on a few SMs.  ``defer_tokens`` trades latency for parallelism:
 passes are queued and hashed together once that many tokens are pending (or
-at ``flush`` / ``close``).  Deferred passes are read at flush time, so their
-capture buffers must stay valid until then; wrap tensors (logits, final
-residuals, lp hidden) are read in place when every queued pass uses the same
-tensor (a ring buffer with per-token rows), and gathered otherwise.
+at ``flush`` / ``close``).  Deferring is the default (``DEFAULT_DEFER_TOKENS``,
+8 192 tokens: 32 decode steps of a 256-sequence batch), which keeps both the
+long leaves and the serial IO chain off the decode step and off the
+post-generation critical path; ``defer_tokens=0`` hashes every pass as it is
+stepped.  Deferred passes are read at flush time, so their capture buffers
+must stay valid until then: a caller that reuses capture buffers keeps at
+least ``ceil(defer_tokens / tokens per pass)`` of them in a ring, or calls
+``flush`` before overwriting one.  Wrap tensors (logits, final residuals, lp
+hidden) are read in place when every queued pass uses the same tensor (a ring
+buffer with per-token rows), and gathered otherwise.
 """
 from __future__ import annotations
 
@@ -29,6 +35,8 @@ import torch
 
 from . import commit as C
 from ._lib import check, lib
+
+DEFAULT_DEFER_TOKENS = 8192
 
 
 @dataclass
@@ -118,12 +126,13 @@ class OnlineCommitter:
 
     ``max_slots`` requests can be open at once, each with at most
     ``max_tokens`` committed tokens (``token_ids = all_ids[1:]`` in the
-    reference, i.e. one per forward-pass row).  ``defer_tokens``: 0 hashes
-    every pass when it is stepped; N > 0 queues passes until N tokens are
-    pending (see the module docstring).
+    reference, i.e. one per forward-pass row).  ``defer_tokens``: N > 0
+    queues passes until N tokens are pending (default
+    ``DEFAULT_DEFER_TOKENS``; see the module docstring for the capture
+    lifetime this requires); 0 hashes every pass when it is stepped.
     """
 
-    def __init__(self, ctx: C.Context, max_slots: int, max_tokens: int, defer_tokens: int = 0):
+    def __init__(self, ctx: C.Context, max_slots: int, max_tokens: int, defer_tokens: int = DEFAULT_DEFER_TOKENS):
         self.ctx = ctx
         self.max_slots, self.max_tokens = int(max_slots), int(max_tokens)
         self.defer_tokens = int(defer_tokens)

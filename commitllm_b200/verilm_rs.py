@@ -223,7 +223,7 @@ class _Committed:
         self._seed = bytes(seed)
         self._layout = layout            # where each token's retained rows live on the device
         self._n_tokens = n_tokens
-        self._token_ids = list(token_ids)
+        self._token_src = token_ids     # host sequence or device tensor, read on demand
         self._n_prompt_tokens = n_prompt_tokens
         self._digests = digests          # device [4 + ..., 32]: trace root, io root, prompt hash, seed commitment
         self._trees = trees              # TreeSet: tree 0 trace, tree 1 io
@@ -232,6 +232,16 @@ class _Committed:
         self._n_kv_layers = n_kv_layers
         self._kv_view = None
         self._host = None
+
+    @property
+    def _token_ids(self) -> List[int]:
+        if not isinstance(self._token_src, list):
+            t = self._token_src
+            if isinstance(t, torch.Tensor):
+                self._ctx.sync()
+                t = t.cpu().numpy().view(np.uint32)
+            self._token_src = [int(x) for x in t]
+        return self._token_src
 
     def _h(self):
         if self._host is None:
@@ -284,6 +294,7 @@ class _Committed:
     # --- openings (merkle::prove over the committed trees) ---
     def _proof(self, trees: C.TreeSet, tree: int, index: int):
         sib, depth = trees.prove([tree], [index])
+        self._ctx.sync()
         s = sib[0, :depth[0]].cpu().numpy()
         return {"leaf_index": int(index), "siblings": [bytes(x).hex() for x in s]}
 
@@ -373,6 +384,7 @@ class _Committed:
         if not leaves:
             return []
         sib, depth = trees.prove([tree] * len(leaves), list(leaves))
+        self._ctx.sync()
         s = sib.cpu().numpy()
         return [{"leaf_index": int(j), "siblings": [bytes(x) for x in s[k, :depth[k]]]} for k, j in enumerate(leaves)]
 
@@ -388,6 +400,7 @@ class _Committed:
             raise ValueError(f"token_index {token_index} out of range (n_tokens={self._n_tokens})")
         if self._layout is None:
             raise ValueError("this handle keeps no capture layout to open")
+        self._ctx.sync()
         leaves = self._trees.nodes(0)[: self._n_tokens].cpu().numpy()
         ios = self._trees.nodes(1)[: self._n_tokens].cpu().numpy()
         if i == 0:
@@ -471,29 +484,44 @@ def _check_common(token_ids, sampling_seed, manifest):
 def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens, kv_cache, handle_cls,
             manifest=None, **extra):
     n = len(layout.tok_fwd)
-    if n != len(token_ids):
+    n_ids = token_ids.numel() if isinstance(token_ids, torch.Tensor) else len(token_ids)
+    if n != n_ids:
         raise ValueError("retained state count must match token_ids")
     if n == 0:
         raise ValueError("need at least one leaf")
+    kv_roots = kv_trees = None
+    n_kv_layers = 0
+    side = None
+    if kv_cache is not None:
+        if len(kv_cache.seq_lens) != 1:
+            raise ValueError("kv_cache must describe exactly the request's one sequence")
+        # the KV trees run on a second stream, beside the trace leaves and the IO chain:
+        # for one request those are a few thousand serial SHA chains on a few SMs
+        side = ctx.fork()
+        r, kv_trees = C.kv_commit(side, kv_cache, keep_trees=True)
+        kv_trees.ctx = ctx               # later openings run on the main stream, after the join below
+        kv_roots = r[0]
+        n_kv_layers = len(kv_cache.k_layers)
     # leaves and io values in one buffer so both trees build in one launch
     both = ctx.empty(2 * n, 32)
     C.trace_leaves(ctx, layout, out=both[:n])
-    tok = ctx.to_device(np.asarray([int(t) for t in token_ids], dtype=np.uint32).view(np.int32))
+    if isinstance(token_ids, torch.Tensor) and token_ids.is_cuda:
+        if token_ids.dtype not in (torch.int32, torch.uint32) or token_ids.numel() != n:
+            raise ValueError("token_ids on the device must be a 32-bit tensor of n_tokens entries")
+        tok = token_ids.reshape(-1).contiguous()
+    else:
+        tok = ctx.to_device(np.asarray([int(t) for t in token_ids], dtype=np.uint32).view(np.int32))
     digests = ctx.empty(4, 32)
     ph = C.prompt_hashes(ctx, [bytes(prompt)])
     C.io_chain(ctx, both[:n], tok, ph, [0, n], out=both[n:])
     roots, trees = C.build_trees(ctx, both, [0, n, 2 * n], keep_trees=True, roots_out=digests[:2])
-    digests[2].copy_(ph[0])
     seeds = ctx.to_device(np.frombuffer(seed, dtype=np.uint8).reshape(1, 32))
-    digests[3:4].copy_(C.seed_commitments(ctx, seeds))
-    kv_roots = kv_trees = None
-    n_kv_layers = 0
-    if kv_cache is not None:
-        if len(kv_cache.seq_lens) != 1:
-            raise ValueError("kv_cache must describe exactly the request's one sequence")
-        r, kv_trees = C.kv_commit(ctx, kv_cache, keep_trees=True)
-        kv_roots = r[0]
-        n_kv_layers = len(kv_cache.k_layers)
+    sc = C.seed_commitments(ctx, seeds)
+    with torch.cuda.stream(ctx.stream):
+        digests[2].copy_(ph[0])
+        digests[3:4].copy_(sc)
+    if side is not None:
+        ctx.join(side)
     h = handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers,
                    manifest=manifest, prompt=prompt, seed=seed, layout=layout, **extra)
     h._kv_view = kv_cache
@@ -639,5 +667,61 @@ def commit_minimal_packed(packed_a, packed_scales, n_layers, hidden_dim, fwd_bat
         lay.tok_fr_row = list(range(n_tok))
         keep.append(fr)
     h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, PackedBatchStateHandle, manifest=man)
+    h._inputs = keep
+    return h
+
+
+def commit_request(a: torch.Tensor, scales_a: torch.Tensor, token_ids, prompt, sampling_seed, *,
+                   n_prompt_tokens: Optional[int] = None, captured_logits_f32: Optional[torch.Tensor] = None,
+                   kv_cache: Optional[C.KvCacheView] = None, manifest=None,
+                   ctx: Optional[C.Context] = None) -> MinimalBatchStateHandle:
+    """One request's whole commitment, from captures already in device memory.
+
+    An entry of this library with no PyO3 counterpart: it makes the commitment
+    ``commit_minimal_from_captures`` makes (``commit_minimal``,
+    prover/src/lib.rs:336-544: trace leaves, IO chain, trace and IO trees,
+    manifest hashes, KV trees), but takes the captures as whole tensors, so a
+    long request costs a handful of launches and no per-entry host work; the
+    KV trees run on a second stream beside the trace leaves and the serial IO
+    chain.
+
+    a: int8 ``[n_tokens, n_layers, hidden]`` (the o_proj input row of each
+    committed token and layer, token order); scales_a: float32
+    ``[n_tokens, n_layers]``; token_ids: ``n_tokens`` ids (``all_ids[1:]``, a
+    host sequence or a 32-bit CUDA tensor); captured_logits_f32: float32
+    ``[rows, vocab]``, row j bound to token ``gen_start + j`` with
+    ``gen_start = n_prompt_tokens - 1`` (prover/src/lib.rs:367-390);
+    kv_cache: the request's K/V rows (one sequence).
+    """
+    ctx = ctx or C.Context()
+    C._require_cuda(a, "a")
+    C._require_cuda(scales_a, "scales_a")
+    if a.dtype not in (torch.int8, torch.uint8) or a.dim() != 3 or not a.is_contiguous():
+        raise ValueError("a must be a contiguous int8 [n_tokens, n_layers, hidden] CUDA tensor")
+    n, L, H = (int(x) for x in a.shape)
+    if scales_a.dtype != torch.float32 or tuple(scales_a.shape) != (n, L) or not scales_a.is_contiguous():
+        raise ValueError(f"scales_a must be a contiguous float32 [{n}, {L}] CUDA tensor")
+    ids = token_ids if isinstance(token_ids, torch.Tensor) else list(token_ids)
+    if isinstance(ids, list):
+        seed, man = _check_common(ids, sampling_seed, manifest)
+    else:
+        seed, man = _check_common([], sampling_seed, manifest)
+    # every token its own one-row pass: row pointers of token t, layer l
+    tl = np.arange(n, dtype=np.uint64)[:, None] * np.uint64(L) + np.arange(L, dtype=np.uint64)[None, :]
+    lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=np.ones(n, np.int32), tok_fwd=np.arange(n, dtype=np.int32),
+                        tok_row=np.zeros(n, np.int32), a_rows=np.uint64(a.data_ptr()) + tl * np.uint64(H),
+                        scale_a=np.uint64(scales_a.data_ptr()) + tl * np.uint64(4), scale_stride=1)
+    keep = [a, scales_a]
+    if captured_logits_f32 is not None:
+        C._require_cuda(captured_logits_f32, "captured_logits_f32")
+        lg = captured_logits_f32
+        if lg.dtype != torch.float32 or lg.dim() != 2 or lg.stride(1) != 1:
+            raise ValueError("captured_logits_f32 must be a float32 [rows, vocab] CUDA tensor with unit column stride")
+        gen_start = max(0, n_prompt_tokens - 1) if n_prompt_tokens is not None else 0
+        t = np.arange(n, dtype=np.int64) - gen_start
+        lay.logits = lg
+        lay.tok_logits_row = np.where((t >= 0) & (t < lg.shape[0]), t, -1).astype(np.int32)
+        keep.append(lg)
+    h = _finish(ctx, lay, ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle, manifest=man)
     h._inputs = keep
     return h

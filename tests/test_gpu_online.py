@@ -103,3 +103,47 @@ def test_online_rejects_bad_steps(ctx):
         oc.step([0, 0, 0], lay, ctx.to_device(np.zeros(3, np.int32)))   # exceeds max_tokens
     with pytest.raises(ValueError):
         oc.step([0, 1, 0], lay, ctx.to_device(np.zeros(3, np.int32)))   # slot 1 not open
+
+
+def test_deferred_default_with_a_capture_ring(ctx):
+    """The capture-lifetime contract of deferred mode: a decode loop that reuses
+    ceil(defer_tokens / tokens per pass) capture buffers in a ring never has one
+    overwritten before the flush that reads it, so the roots equal the offline
+    commit; the default committer (DEFAULT_DEFER_TOKENS) defers every pass."""
+    from commitllm_b200 import online
+    assert OnlineCommitter(ctx, max_slots=1, max_tokens=1).defer_tokens == online.DEFAULT_DEFER_TOKENS > 0
+    B, steps, defer = 4, 11, 12                  # 3 passes per flush
+    depth = -(-defer // B)
+    oc = OnlineCommitter(ctx, max_slots=B, max_tokens=steps, defer_tokens=defer)
+    for s in range(B):
+        oc.open(s, b"ring %d" % s, bytes([s + 1]) * 32, n_prompt_tokens=1)
+    ring_a = [ctx.empty(L, B, H, dtype=torch.int8) for _ in range(depth)]
+    ring_s = [ctx.empty(L, B, dtype=torch.float32) for _ in range(depth)]
+    ring_l = ctx.empty(depth * B, V, dtype=torch.float32)   # logits rows of the ring's passes
+    rng = np.random.default_rng(11)
+    hist = {s: [] for s in range(B)}
+    for k in range(steps):
+        slot = k % depth
+        a = rng.integers(-128, 128, size=(L, B, H), dtype=np.int8)
+        sc = rng.random((L, B), dtype=np.float32)
+        lg = rng.standard_normal((B, V)).astype(np.float32)
+        toks = rng.integers(0, 1000, size=B).astype(np.int32)
+        with torch.cuda.stream(ctx.stream):
+            ring_a[slot].copy_(torch.from_numpy(a))
+            ring_s[slot].copy_(torch.from_numpy(sc))
+            ring_l[slot * B:(slot + 1) * B].copy_(torch.from_numpy(lg))
+        for s in range(B):
+            hist[s].append((a[:, s].copy(), sc[:, s].copy(), lg[s].copy(), int(toks[s])))
+        lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[B], tok_fwd=[0] * B, tok_row=list(range(B)),
+                            a_rows=[[ring_a[slot].data_ptr() + l * B * H for l in range(L)]],
+                            scale_a=[[ring_s[slot].data_ptr() + 4 * l * B for l in range(L)]], scale_stride=1,
+                            logits=ring_l, tok_logits_row=[slot * B + s for s in range(B)])
+        oc.step(list(range(B)), lay, ctx.to_device(toks))
+    res = {s: oc.close(s) for s in range(B)}
+    ctx.sync(timeout_ms=60000)
+    for s in range(B):
+        retained = [[O.RetainedLayerState(h[0][l].tobytes(), float(h[1][l])) for l in range(L)] for h in hist[s]]
+        com = O.commit_minimal(retained, [h[3] for h in hist[s]], b"ring %d" % s, bytes([s + 1]) * 32,
+                               captured_logits_f32=[h[2] for h in hist[s]], n_prompt_tokens=1)
+        assert bytes(res[s]["merkle_root"].cpu().numpy()) == com.merkle_root
+        assert bytes(res[s]["io_root"].cpu().numpy()) == com.io_root

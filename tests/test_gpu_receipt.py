@@ -142,3 +142,24 @@ def test_audit_without_kv_and_bad_index(ctx):
     assert resp["kv_entries"] is None and resp["kv_proofs"] is None
     with pytest.raises(ValueError, match="out of range"):
         h.audit_v4_binary(C1["n_tokens"])
+
+
+def test_commit_request_equals_the_from_captures_commit(ctx):
+    """commit_request (whole tensors, KV trees on a second stream) makes the same
+    commitment and the same receipts as commit_minimal_from_captures."""
+    import torch
+    from commitllm_b200 import receipt as R
+    h1, (k, v, tok, a, sc, logits) = _commit(ctx)
+    n = C1["n_tokens"]
+    view = kvref.Transcript(k, v, [n], VC_DTYPE_BF16).view(ctx.device)
+    A = ctx.to_device(np.ascontiguousarray(a)).view(torch.int8)
+    S = ctx.to_device(np.ascontiguousarray(sc, dtype=np.float32))
+    LG = ctx.to_device(np.stack(logits).astype(np.float32))
+    T = ctx.to_device(np.asarray(tok, dtype=np.int32))
+    h2 = V.commit_request(A, S, T, C1["prompt"].encode(), bytes.fromhex(C1["sampling_seed"]), n_prompt_tokens=3,
+                          captured_logits_f32=LG, kv_cache=view, manifest=MANIFEST, ctx=ctx)
+    assert h2.commitment_json() == h1.commitment_json()
+    for t in (0, 77):
+        r1 = R.zstd_decompress(h1.audit_v4_binary(t, layer_indices=[0])[4:])
+        r2 = R.zstd_decompress(h2.audit_v4_binary(t, layer_indices=[0])[4:])
+        assert r1 == r2

@@ -253,7 +253,7 @@ def test_verilm_rs_argument_errors(ctx):
         V.commit_minimal_from_captures([b"\0" * 4], np.zeros(4, np.float32), 1, [1], [1, 2], b"p", b"\0" * 32, ctx=ctx)
     with pytest.raises(ValueError, match="packed_a"):
         V.commit_minimal_packed(b"\0" * 5, np.zeros(4, np.float32), 1, 4, [1], [1], b"p", b"\0" * 32, ctx=ctx)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="manifest missing tokenizer_hash"):   # extract_manifest, lib.rs:174-178
         V.commit_minimal_from_captures([b"\0" * 4], np.zeros(4, np.float32), 1, [1], [1], b"p", b"\0" * 32,
                                        manifest={"x": 1}, ctx=ctx)
 

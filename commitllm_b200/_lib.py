@@ -22,7 +22,7 @@ SYMBOLS = (
     "vc_kv_commit", "vc_trace_leaves", "vc_io_chain", "vc_prompt_hash", "vc_seed_commitment",
     "vc_build_trees", "vc_prove", "vc_tree_set_count", "vc_tree_nodes", "vc_tree_set_free",
     "vc_int_peak", "vc_kv_commit_noalloc", "vc_kv_open", "vc_io_extend", "vc_io_genesis",
-    "vc_kv_transcript",
+    "vc_kv_transcript", "vc_kv_transcript_commit",
 )
 
 
@@ -111,6 +111,7 @@ def _declare(lib):
         "vc_kv_open": [P, POINTER(KvDesc), P, c_int32, c_int32, POINTER(c_int32), c_int32, P, P, c_int32,
                        POINTER(c_int32)],
         "vc_kv_transcript": [P, POINTER(KvtDesc), P, P],
+        "vc_kv_transcript_commit": [P, POINTER(KvtDesc), c_int32, P, POINTER(P)],
     }.items():
         fn = getattr(lib, name)
         fn.restype = c_int32

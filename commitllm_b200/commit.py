@@ -605,9 +605,8 @@ class KvTranscriptInputs:
     rope: Optional[RopeConfig] = None
 
 
-def kv_transcript(ctx: Context, inp: KvTranscriptInputs, k_out: Optional[torch.Tensor] = None,
-                  v_out: Optional[torch.Tensor] = None):
-    """``k_roped, v_deq``: float64 ``[n_layers, n_tokens, kv_dim]`` device tensors."""
+def _kvt_desc(inp: KvTranscriptInputs):
+    """(vc_kvt_desc, arrays it points to, n_layers, n_tokens, kv_dim) of the inputs."""
     xs = list(inp.x_attn) if not isinstance(inp.x_attn, torch.Tensor) else [x for x in inp.x_attn]
     n_layers = len(xs)
     if n_layers < 1 or len(inp.wk) != n_layers or len(inp.wv) != n_layers:
@@ -675,6 +674,13 @@ def kv_transcript(ctx: Context, inp: KvTranscriptInputs, k_out: Optional[torch.T
         d.rope_original_max_position_embeddings = int(r.original_max_position_embeddings)
         d.rope_factor, d.rope_low_freq_factor = float(r.factor), float(r.low_freq_factor)
         d.rope_high_freq_factor = float(r.high_freq_factor)
+    return d, keep, n_layers, n_tok, kv
+
+
+def kv_transcript(ctx: Context, inp: KvTranscriptInputs, k_out: Optional[torch.Tensor] = None,
+                  v_out: Optional[torch.Tensor] = None):
+    """``k_roped, v_deq``: float64 ``[n_layers, n_tokens, kv_dim]`` device tensors."""
+    d, keep, n_layers, n_tok, kv = _kvt_desc(inp)
     if k_out is None:
         k_out = ctx.empty(n_layers, n_tok, kv, dtype=torch.float64)
     if v_out is None:
@@ -685,6 +691,26 @@ def kv_transcript(ctx: Context, inp: KvTranscriptInputs, k_out: Optional[torch.T
     check(lib().vc_kv_transcript(ctx.handle, ctypes.byref(d), ctypes.c_void_p(k_out.data_ptr()),
                                  ctypes.c_void_p(v_out.data_ptr())))
     return k_out, v_out
+
+
+def kv_transcript_commit(ctx: Context, inp: KvTranscriptInputs, layer_base: int = 0, keep_trees: bool = True,
+                         roots_out: Optional[torch.Tensor] = None):
+    """The per-layer kv_roots of the transcript of ``inp`` (positions 0..n_tokens-1,
+    leaf layer index ``layer_base + l``), with the K/V rows hashed as they are
+    computed and never stored: the roots and trees of :func:`kv_transcript`
+    followed by :func:`kv_commit` of its rows.  Returns ``(roots [n_layers,
+    32], TreeSet or None)`` (tree index = layer)."""
+    d, keep, n_layers, n_tok, kv = _kvt_desc(inp)
+    if roots_out is None:
+        roots_out = ctx.empty(n_layers, 32)
+    if roots_out.numel() < n_layers * 32 or not roots_out.is_contiguous():
+        raise ValueError("roots_out too small or not contiguous")
+    h = ctypes.c_void_p()
+    check(lib().vc_kv_transcript_commit(ctx.handle, ctypes.byref(d), int(layer_base),
+                                        ctypes.c_void_p(roots_out.data_ptr()),
+                                        ctypes.byref(h) if keep_trees else None))
+    del keep
+    return roots_out.view(n_layers, 32), (TreeSet(ctx, h) if keep_trees else None)
 
 
 def kv_transcript_view(k: torch.Tensor, v: torch.Tensor, layer_base: int = 0) -> KvCacheView:

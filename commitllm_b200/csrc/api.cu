@@ -856,32 +856,39 @@ vc_status vc_seed_commitment(vc_ctx* c, int32_t n, const uint8_t* seeds_dev, uin
 
 // ------------------------------------------------------------ KV transcript
 
-vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, double* v_out) {
-  if (!c || !d) return fail(VC_EINVAL, "vc_kv_transcript: NULL argument");
+}  // extern "C"
+
+namespace {
+
+// Argument checks of the transcript entry points (n_tokens >= 0).
+vc_status check_kvt(const vc_kvt_desc* d, const char* fn) {
   if (d->n_tokens < 0 || d->n_layers < 1 || d->n_kv_heads < 1)
-    return fail(VC_EINVAL, "vc_kv_transcript: n_tokens >= 0, n_layers and n_kv_heads >= 1 required");
-  if (d->hidden < 16 || d->hidden % 16) return fail(VC_EINVAL, "vc_kv_transcript: hidden %d must be a positive multiple of 16", d->hidden);
+    return fail(VC_EINVAL, "%s: n_tokens >= 0, n_layers and n_kv_heads >= 1 required", fn);
+  if (d->hidden < 16 || d->hidden % 16) return fail(VC_EINVAL, "%s: hidden %d must be a positive multiple of 16", fn, d->hidden);
   if (d->head_dim < 2 || d->head_dim % 2 || d->head_dim > 256)
-    return fail(VC_EINVAL, "vc_kv_transcript: head_dim %d must be even and <= 256", d->head_dim);
+    return fail(VC_EINVAL, "%s: head_dim %d must be even and <= 256", fn, d->head_dim);
   const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
-  if (kv > (int64_t(1) << 24)) return fail(VC_EINVAL, "vc_kv_transcript: kv_dim too large");
+  if (kv > (int64_t(1) << 24)) return fail(VC_EINVAL, "%s: kv_dim too large", fn);
   if (d->n_tokens == 0) return VC_OK;
-  if (!k_out || !v_out) return fail(VC_EINVAL, "vc_kv_transcript: NULL output");
   if (d->x_row_stride < d->hidden || d->x_row_stride % 16)
-    return fail(VC_EINVAL, "vc_kv_transcript: x_row_stride must be >= hidden and a multiple of 16");
-  if (!d->x_layers || !d->wk_layers || !d->wv_layers) return fail(VC_EINVAL, "vc_kv_transcript: NULL layer table");
-  if (d->use_rope && !d->scale_x) return fail(VC_EINVAL, "vc_kv_transcript: scale_x is NULL");
-  if (reinterpret_cast<uintptr_t>(k_out) % 32 || reinterpret_cast<uintptr_t>(v_out) % 32)
-    return fail(VC_EINVAL, "vc_kv_transcript: outputs must be 32-byte aligned");
+    return fail(VC_EINVAL, "%s: x_row_stride must be >= hidden and a multiple of 16", fn);
+  if (!d->x_layers || !d->wk_layers || !d->wv_layers) return fail(VC_EINVAL, "%s: NULL layer table", fn);
+  if (d->use_rope && !d->scale_x) return fail(VC_EINVAL, "%s: scale_x is NULL", fn);
   for (int l = 0; l < d->n_layers; ++l) {
     const void* p[3] = {d->x_layers[l], d->wk_layers[l], d->wv_layers[l]};
     for (const void* q : p)
       if (!q || reinterpret_cast<uintptr_t>(q) % 16)
-        return fail(VC_EINVAL, "vc_kv_transcript: x/Wk/Wv pointer of layer %d is NULL or not 16-byte aligned", l);
+        return fail(VC_EINVAL, "%s: x/Wk/Wv pointer of layer %d is NULL or not 16-byte aligned", fn, l);
   }
-  DeviceGuard g(c->device);
+  return VC_OK;
+}
 
-  // (cos, sin) table: built once per frequency set on the host (C library cos/sin)
+// The context's (cos, sin) table for these frequencies and >= n_tokens
+// positions (host C library cos/sin), then the per-layer tensor maps (x_attn
+// boxes of 128 rows, weight boxes of w_box_rows rows) and scale/bias tables,
+// staged to the device; fills every field of *a except out[] and err.
+vc_status prepare_kvt(vc_ctx* c, const vc_kvt_desc* d, int w_box_rows, KvtArgs* a, const char* fn) {
+  const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
   if (d->use_rope) {
     const std::vector<double> inv =
         kvt_inv_freq(d->head_dim, d->rope_theta, d->rope_scaling, d->rope_factor, d->rope_low_freq_factor,
@@ -898,21 +905,19 @@ vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, doubl
       c->rope_rows = 0;
       c->rope_inv.clear();
       if (cudaMalloc(&c->rope, tab.size() * sizeof(double)) != cudaSuccess)
-        return fail(VC_ENOMEM, "vc_kv_transcript: RoPE table of %zu bytes", tab.size() * sizeof(double));
+        return fail(VC_ENOMEM, "%s: RoPE table of %zu bytes", fn, tab.size() * sizeof(double));
       VC_CUDA(cudaMemcpy(c->rope, tab.data(), tab.size() * sizeof(double), cudaMemcpyHostToDevice));
       c->rope_rows = rows;
       c->rope_inv = inv;
     }
   }
-
-  // tensor maps (x_attn, Wk, Wv per layer) and per-layer scale/bias tables
   std::vector<CUtensorMap> maps(size_t(d->n_layers) * 3);
   std::vector<KvtLayer> layers(d->n_layers);
   for (int l = 0; l < d->n_layers; ++l) {
     int r = kvt_encode_map(&maps[3 * l], d->x_layers[l], d->hidden, d->n_tokens, d->x_row_stride, 128);
-    if (!r) r = kvt_encode_map(&maps[3 * l + 1], d->wk_layers[l], d->hidden, kv, d->hidden, 256);
-    if (!r) r = kvt_encode_map(&maps[3 * l + 2], d->wv_layers[l], d->hidden, kv, d->hidden, 256);
-    if (r) return fail(VC_ECUDA, "vc_kv_transcript: cuTensorMapEncodeTiled failed (%d) for layer %d", r, l);
+    if (!r) r = kvt_encode_map(&maps[3 * l + 1], d->wk_layers[l], d->hidden, kv, d->hidden, w_box_rows);
+    if (!r) r = kvt_encode_map(&maps[3 * l + 2], d->wv_layers[l], d->hidden, kv, d->hidden, w_box_rows);
+    if (r) return fail(VC_ECUDA, "%s: cuTensorMapEncodeTiled failed (%d) for layer %d", fn, r, l);
     KvtLayer& L = layers[l];
     std::memset(&L, 0, sizeof(L));
     L.ch[0] = d->ch_k ? d->ch_k[l] : nullptr;
@@ -928,32 +933,132 @@ vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, doubl
   char* dev = nullptr;
   vc_status r = upload(c, st, &dev);
   if (r) return r;
+  std::memset(a, 0, sizeof(*a));
+  a->maps = reinterpret_cast<const CUtensorMap*>(dev + om);
+  a->layers = reinterpret_cast<const KvtLayer*>(dev + ol);
+  a->scale_x = d->scale_x;
+  a->sx_t = d->sx_tstride;
+  a->sx_l = d->sx_lstride;
+  a->rope = d->use_rope ? reinterpret_cast<const double2*>(c->rope) : nullptr;
+  a->rope_rows = c->rope_rows;
+  a->n_tokens = d->n_tokens;
+  a->hidden = d->hidden;
+  a->kv_dim = int32_t(kv);
+  a->head_dim = d->head_dim;
+  a->use_rope = d->use_rope != 0;
+  a->err = c->err;
+  a->m_tiles = (d->n_tokens + 127) / 128;
+  return VC_OK;
+}
 
+}  // namespace
+
+extern "C" {
+
+vc_status vc_kv_transcript(vc_ctx* c, const vc_kvt_desc* d, double* k_out, double* v_out) {
+  if (!c || !d) return fail(VC_EINVAL, "vc_kv_transcript: NULL argument");
+  vc_status r = check_kvt(d, "vc_kv_transcript");
+  if (r || d->n_tokens == 0) return r;
+  if (!k_out || !v_out) return fail(VC_EINVAL, "vc_kv_transcript: NULL output");
+  if (reinterpret_cast<uintptr_t>(k_out) % 32 || reinterpret_cast<uintptr_t>(v_out) % 32)
+    return fail(VC_EINVAL, "vc_kv_transcript: outputs must be 32-byte aligned");
+  DeviceGuard g(c->device);
   KvtArgs a;
-  std::memset(&a, 0, sizeof(a));
-  a.maps = reinterpret_cast<const CUtensorMap*>(dev + om);
-  a.layers = reinterpret_cast<const KvtLayer*>(dev + ol);
-  a.scale_x = d->scale_x;
-  a.sx_t = d->sx_tstride;
-  a.sx_l = d->sx_lstride;
-  a.rope = d->use_rope ? reinterpret_cast<const double2*>(c->rope) : nullptr;
-  a.rope_rows = c->rope_rows;
+  r = prepare_kvt(c, d, 256, &a, "vc_kv_transcript");
+  if (r) return r;
   a.out[0] = k_out;
   a.out[1] = v_out;
-  a.n_tokens = d->n_tokens;
-  a.hidden = d->hidden;
-  a.kv_dim = int32_t(kv);
-  a.head_dim = d->head_dim;
   a.tile_cols = (256 / d->head_dim) * d->head_dim;
-  a.tiles_per_mat = int32_t((kv + a.tile_cols - 1) / a.tile_cols);
-  a.use_rope = d->use_rope != 0;
-  a.err = c->err;
-  a.m_tiles = (d->n_tokens + 127) / 128;
+  a.tiles_per_mat = int32_t((int64_t(a.kv_dim) + a.tile_cols - 1) / a.tile_cols);
   const int64_t n_tiles = int64_t(d->n_layers) * a.m_tiles * 2 * a.tiles_per_mat;
   if (n_tiles > 0x7FFFFFFF) return fail(VC_EINVAL, "vc_kv_transcript: too many tiles");
   a.n_tiles = int32_t(n_tiles);
   const cudaError_t e = launch_kv_transcript(a, c->n_sm, c->stream);
   if (e != cudaSuccess) return fail(VC_ECUDA, "vc_kv_transcript launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
+vc_status vc_kv_transcript_commit(vc_ctx* c, const vc_kvt_desc* d, int32_t layer_base, uint8_t* kv_roots_dev,
+                                  vc_tree_set** trees_out) {
+  if (!c || !d || !kv_roots_dev) return fail(VC_EINVAL, "vc_kv_transcript_commit: NULL argument");
+  vc_status r = check_kvt(d, "vc_kv_transcript_commit");
+  if (r) return r;
+  if (d->n_tokens < 1) return fail(VC_EINVAL, "vc_kv_transcript_commit: need at least one position (build_tree)");
+  if (layer_base < 0 || int64_t(layer_base) + d->n_layers > 0x7FFFFFFF)
+    return fail(VC_EINVAL, "vc_kv_transcript_commit: layer_base %d out of range", layer_base);
+  DeviceGuard g(c->device);
+  const int64_t kv = int64_t(d->n_kv_heads) * d->head_dim;
+  if (!kvt_commit_supported(d->head_dim, int(kv))) {
+    // Other head sizes: the transcript's f64 rows through device scratch, then their trees.
+    const size_t bytes = size_t(d->n_layers) * size_t(d->n_tokens) * size_t(kv) * sizeof(double);
+    double* kbuf = nullptr;
+    double* vbuf = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&kbuf), bytes, c->stream) != cudaSuccess ||
+        cudaMallocAsync(reinterpret_cast<void**>(&vbuf), bytes, c->stream) != cudaSuccess) {
+      if (kbuf) cudaFreeAsync(kbuf, c->stream);
+      return fail(VC_ENOMEM, "vc_kv_transcript_commit: f64 rows of %zu bytes", 2 * bytes);
+    }
+    r = vc_kv_transcript(c, d, kbuf, vbuf);
+    if (!r) {
+      std::vector<const void*> kl(d->n_layers), vl(d->n_layers);
+      for (int l = 0; l < d->n_layers; ++l) {
+        kl[l] = kbuf + size_t(l) * d->n_tokens * kv;
+        vl[l] = vbuf + size_t(l) * d->n_tokens * kv;
+      }
+      const int32_t n = d->n_tokens;
+      vc_kv_desc kd{};
+      kd.n_layers = d->n_layers;
+      kd.layer_base = layer_base;
+      kd.n_kv_heads = 1;
+      kd.head_dim = int32_t(kv);
+      kd.dtype = VC_DTYPE_F64;
+      kd.n_seqs = 1;
+      kd.seq_lens = &n;
+      kd.stride_row = kv;
+      kd.stride_head = kv;
+      kd.cache_elems = int64_t(n) * kv;
+      kd.k_layers = kl.data();
+      kd.v_layers = vl.data();
+      r = vc_kv_commit(c, &kd, kv_roots_dev, trees_out);
+    }
+    cudaFreeAsync(kbuf, c->stream);
+    cudaFreeAsync(vbuf, c->stream);
+    return r;
+  }
+  KvtcArgs A;
+  std::memset(&A, 0, sizeof(A));
+  r = prepare_kvt(c, d, 128, &A.t, "vc_kv_transcript_commit");
+  if (r) return r;
+  const int64_t n_units = int64_t(d->n_layers) * A.t.m_tiles;
+  if (n_units > 0x7FFFFFFF) return fail(VC_EINVAL, "vc_kv_transcript_commit: too many units");
+  A.n_units = int32_t(n_units);
+  A.layer_base = layer_base;
+  Plan p;
+  plan_group(p, d->n_tokens, d->n_layers, 0, 0);
+  A.meta = p.meta[0];
+  vc_tree_set* ts = nullptr;
+  if (trees_out) {
+    r = make_tree_set(c, p, d->n_layers, &ts);
+    if (r) return r;
+  }
+  const size_t counters_bytes = align_up(sizeof(uint32_t) * p.n_trees, 256);
+  const size_t croot_bytes = ts ? 0 : size_t(p.croots) * 32;
+  r = ensure_scratch(c, counters_bytes + croot_bytes);
+  if (!r) {
+    A.out.nodes = ts ? ts->nodes : nullptr;
+    A.out.counters = reinterpret_cast<uint32_t*>(c->scratch);
+    A.out.croots = c->scratch + counters_bytes;
+    A.out.roots = kv_roots_dev;
+    A.out.zero_roots = c->zero_roots;
+    cudaError_t e = cudaMemsetAsync(c->scratch, 0, counters_bytes, c->stream);
+    if (e == cudaSuccess) e = launch_kvt_commit(A, c->n_sm, c->stream);
+    if (e != cudaSuccess) r = fail(VC_ECUDA, "vc_kv_transcript_commit launch: %s", cudaGetErrorString(e));
+  }
+  if (r) {
+    if (ts) vc_tree_set_free(ts);
+    return r;
+  }
+  if (trees_out) *trees_out = ts;
   return VC_OK;
 }
 

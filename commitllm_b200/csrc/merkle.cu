@@ -15,6 +15,7 @@
 // hold only zero padding are never launched: their subtree root is the
 // constant Z_k (Z_0 = 0^32, Z_{k+1} = hash_pair(Z_k, Z_k)), which is exactly
 // what build_tree computes for them.
+#include "merkle_tree.cuh"
 #include "sha256_core.cuh"
 #include "sha256_stream.cuh"
 #include "vc_internal.h"
@@ -22,135 +23,6 @@
 #include <cstring>
 
 namespace vc {
-
-__host__ __device__ __forceinline__ int64_t level_off(int lp, int k) {
-  // Nodes before level k in a tree with 2^lp leaves: sum_{i<k} 2^(lp-i).
-  return (int64_t(2) << lp) - (int64_t(2) << (lp - k));
-}
-
-__device__ __forceinline__ void store_z(uint8_t* p, const uint32_t* z) {
-  uint32_t h[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) h[i] = z[i];
-  store_digest(p, h);
-}
-
-// ---------------------------------------------------------------------------
-// Subtree of one chunk, in shared memory.  sd[w][i] is word w of leaf i.
-// ---------------------------------------------------------------------------
-template <int NT>
-__device__ __forceinline__ void chunk_reduce(uint32_t (*sd)[NT], int kc, uint8_t* tnodes, int lp,
-                                             int64_t chunk) {
-  const int tid = threadIdx.x;
-  for (int k = 0; k < kc; ++k) {
-    const int half = 1 << (kc - k - 1);
-    uint32_t out[8];
-    if (tid < half) {
-      uint32_t l[8], r[8];
-#pragma unroll
-      for (int w = 0; w < 8; ++w) { l[w] = sd[w][2 * tid]; r[w] = sd[w][2 * tid + 1]; }
-      hash_pair(l, r, out);
-    }
-    __syncthreads();
-    if (tid < half) {
-#pragma unroll
-      for (int w = 0; w < 8; ++w) sd[w][tid] = out[w];
-      if (tnodes) store_digest(tnodes + (level_off(lp, k + 1) + (chunk << (kc - k - 1)) + tid) * 32, out);
-    }
-    __syncthreads();
-  }
-}
-
-// Levels above the chunks, run by the CTA that finished a tree's last chunk.
-// tnodes: the tree's node array (nullptr in roots-only mode, where tcroot
-// holds the chunk roots and is reduced in place).
-template <int NT>
-__device__ void finish_tree(uint8_t* tnodes, uint8_t* tcroot, int64_t n, int lp, int kc,
-                            int n_chunks, const uint32_t* Z, uint8_t* root_out) {
-  const int tid = threadIdx.x;
-  if (tnodes) {
-    // Zero-padding chunks: every node of theirs at levels 0..kc is Z_k.
-    const int64_t m = int64_t(1) << (lp - kc);
-    for (int k = 0; k <= kc; ++k) {
-      const int64_t per = int64_t(1) << (kc - k);
-      uint8_t* lvl = tnodes + level_off(lp, k) * 32;
-      for (int64_t i = int64_t(n_chunks) * per + tid; i < m * per; i += NT) store_z(lvl + i * 32, Z + 8 * k);
-    }
-  }
-  for (int k = kc; k < lp; ++k) {
-    const int64_t real_k = (n + (int64_t(1) << k) - 1) >> k;
-    const int64_t real_k1 = (n + (int64_t(1) << (k + 1)) - 1) >> (k + 1);
-    const int64_t half = int64_t(1) << (lp - k - 1);
-    const uint8_t* src = tnodes ? tnodes + level_off(lp, k) * 32 : tcroot;
-    uint8_t* dst = tnodes ? tnodes + level_off(lp, k + 1) * 32 : tcroot;
-    const int64_t lim = tnodes ? half : real_k1;
-    for (int64_t base = 0; base < lim; base += NT) {
-      const int64_t i = base + tid;
-      uint32_t out[8];
-      const bool have = i < lim;
-      if (have) {
-        if (i < real_k1) {
-          uint32_t l[8], r[8];
-          load_digest_cg(src + (2 * i) * 32, l);
-          if (2 * i + 1 < real_k) {
-            load_digest_cg(src + (2 * i + 1) * 32, r);
-          } else {
-#pragma unroll
-            for (int w = 0; w < 8; ++w) r[w] = Z[8 * k + w];
-          }
-          hash_pair(l, r, out);
-        } else {
-#pragma unroll
-          for (int w = 0; w < 8; ++w) out[w] = Z[8 * (k + 1) + w];
-        }
-      }
-      __syncthreads();  // in-place mode: every read of this pass precedes the writes
-      if (have) store_digest(dst + i * 32, out);
-    }
-    __syncthreads();
-  }
-  if (tid == 0) {
-    uint32_t r[8];
-    load_digest_cg(tnodes ? tnodes + level_off(lp, lp) * 32 : tcroot, r);
-    store_digest(root_out, r);
-  }
-}
-
-// Common tail of a chunk CTA: reduce, publish, and finish the tree if last.
-template <int NT>
-__device__ __forceinline__ void chunk_tail(uint32_t (*sd)[NT], const TreeMeta& m, int layer,
-                                           int64_t chunk, const TreeOut& o) {
-  __shared__ int s_last;
-  const int tid = threadIdx.x;
-  const int lp = m.log2_pad, kc = m.log2_chunk;
-  uint8_t* tnodes = o.nodes ? o.nodes + (m.node_base + int64_t(layer) * m.node_stride) * 32 : nullptr;
-  uint8_t* tcroot = o.nodes ? nullptr : o.croots + (m.croot_base + int64_t(layer) * m.croot_stride) * 32;
-  const int tree = m.tree_base + layer;
-  chunk_reduce<NT>(sd, kc, tnodes, lp, chunk);
-  if (!tnodes && tid == 0) {
-    uint32_t r[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) r[w] = sd[w][0];
-    store_digest(tcroot + chunk * 32, r);
-  }
-  if (m.n_chunks == 1) {
-    finish_tree<NT>(tnodes, tcroot, m.n_leaves, lp, kc, 1, o.zero_roots, o.roots + int64_t(tree) * 32);
-    return;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(o.counters + tree, 1u);
-    s_last = (prev == unsigned(m.n_chunks - 1));
-  }
-  __syncthreads();
-  if (s_last) {
-    __threadfence();
-    finish_tree<NT>(tnodes, tcroot, m.n_leaves, lp, kc, m.n_chunks, o.zero_roots,
-                    o.roots + int64_t(tree) * 32);
-    if (tid == 0) o.counters[tree] = 0u;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // f64 widening.  The message of hash_kv_entry holds f64le values
@@ -335,6 +207,7 @@ __device__ __forceinline__ int64_t kv_row(const KvArgs& a, const TreeMeta& m, in
 template <int DT>
 __global__ void __launch_bounds__(kTreeThreads) kv_commit_kernel(KvArgs a) {
   __shared__ uint32_t sd[8][kTreeThreads];
+  __shared__ int s_last;
   const int2 it = a.items[blockIdx.x];
   const TreeMeta m = a.meta[it.x];
   const int layer = blockIdx.y;
@@ -368,13 +241,14 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_kernel(KvArgs a) {
     if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + int64_t(layer) * m.node_stride + p) * 32, d);
   }
   __syncthreads();
-  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out, tid, CtaSync(), &s_last);
 }
 
 // Generic path for any kv_dim / head_dim: the stream engine, element by element.
 template <int DT>
 __global__ void __launch_bounds__(kTreeThreads) kv_commit_generic_kernel(KvArgs a) {
   __shared__ uint32_t sd[8][kTreeThreads];
+  __shared__ int s_last;
   __shared__ uint32_t sbuf[16 * kTreeThreads];
   const int2 it = a.items[blockIdx.x];
   const TreeMeta m = a.meta[it.x];
@@ -427,11 +301,12 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_generic_kernel(KvArgs 
     if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + int64_t(layer) * m.node_stride + p) * 32, d);
   }
   __syncthreads();
-  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out, tid, CtaSync(), &s_last);
 }
 
 __global__ void __launch_bounds__(kTreeThreads) tree_commit_kernel(TreeArgs a) {
   __shared__ uint32_t sd[8][kTreeThreads];
+  __shared__ int s_last;
   const int2 it = a.items[blockIdx.x];
   const TreeMeta m = a.meta[it.x];
   const int tid = threadIdx.x;
@@ -451,7 +326,7 @@ __global__ void __launch_bounds__(kTreeThreads) tree_commit_kernel(TreeArgs a) {
     if (a.out.nodes) store_digest(a.out.nodes + (m.node_base + p) * 32, d);
   }
   __syncthreads();
-  chunk_tail<kTreeThreads>(sd, m, 0, chunk, a.out);
+  chunk_tail<kTreeThreads>(sd, m, 0, chunk, a.out, tid, CtaSync(), &s_last);
 }
 
 __global__ void zero_roots_kernel(uint32_t* z) {
@@ -517,6 +392,7 @@ struct NoAllocArgs {
 template <int DT>
 __global__ void __launch_bounds__(kTreeThreads) kv_commit_noalloc_kernel(const __grid_constant__ NoAllocArgs na) {
   __shared__ uint32_t sd[8][kTreeThreads];
+  __shared__ int s_last;
   const KvArgs& a = na.kv;
   int sq = 0;
   while (sq + 1 < na.n_seqs && na.chunk_off[sq + 1] <= int(blockIdx.x)) ++sq;
@@ -551,7 +427,7 @@ __global__ void __launch_bounds__(kTreeThreads) kv_commit_noalloc_kernel(const _
     for (int w = 0; w < 8; ++w) sd[w][tid] = d[w];
   }
   __syncthreads();
-  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out);
+  chunk_tail<kTreeThreads>(sd, m, layer, chunk, a.out, tid, CtaSync(), &s_last);
 }
 
 }  // namespace vc

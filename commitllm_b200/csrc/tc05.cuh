@@ -159,6 +159,16 @@ __device__ __forceinline__ void tmem_ld_wait<16>(uint32_t taddr, uint32_t (&r)[1
 }
 
 template <>
+__device__ __forceinline__ void tmem_ld_wait<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+}
+
+template <>
 __device__ __forceinline__ void tmem_ld2_wait<1>(uint32_t ta, uint32_t tb, uint32_t (&a)[1], uint32_t (&b)[1]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%2];\n\t"

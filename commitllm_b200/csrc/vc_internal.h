@@ -147,6 +147,17 @@ int kvt_encode_map(CUtensorMap* map, const void* base, int64_t inner, int64_t ro
                    int box_rows);
 cudaError_t launch_kv_transcript(const KvtArgs& a, int n_sm, cudaStream_t s);
 
+// kvt_commit.cu: the transcript and its KV trees in one pass (no f64 rows in memory)
+struct KvtcArgs {
+  KvtArgs t;                   // transcript (weight tensor maps with 128-row boxes; out[] unused)
+  TreeMeta meta;               // the n_layers trees over positions 0..n_tokens-1
+  TreeOut out;
+  int32_t layer_base;          // leaf layer index = layer_base + layer
+  int32_t n_units;             // n_layers * m_tiles units of 128 positions
+};
+bool kvt_commit_supported(int head_dim, int kv_dim);
+cudaError_t launch_kvt_commit(const KvtcArgs& a, int n_sm, cudaStream_t s);
+
 // int_peak.cu
 cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,
                             double* ops_per_launch);

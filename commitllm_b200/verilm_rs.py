@@ -108,11 +108,12 @@ class WeightProvider:
 
 def _kv_transcript_from_captures(ctx: C.Context, wp: WeightProvider, x_attn_inputs, scales_d: torch.Tensor,
                                  fwd_batch_sizes, n_layers: int):
-    """``build_retained_from_captures``' x_attn (prover/src/lib.rs:139-181) and
-    ``compute_kv_transcript`` (prover/src/lib.rs:207-329) on the GPU: the
-    captured rows are gathered into ``[n_tokens, layers, hidden]`` on the
-    device, scale_x_attn is the qkv block of each entry's scales
-    (verilm-py/src/lib.rs:859-866).  Returns f64 ``k, v`` ``[layers, n_tokens, kv_dim]``."""
+    """The inputs of ``compute_kv_transcript`` (prover/src/lib.rs:207-329) from
+    the captures: ``build_retained_from_captures``' x_attn (lib.rs:139-181)
+    gathered into ``[n_tokens, layers, hidden]`` on the device, scale_x_attn the
+    qkv block of each entry's scales (verilm-py/src/lib.rs:859-866), the
+    weights, scales, biases and RoPE of the weight provider.  Returns
+    ``(KvTranscriptInputs, tensors to keep alive)``."""
     cfg = wp.config()
     n_entries = len(fwd_batch_sizes) * n_layers
     if len(x_attn_inputs) < n_entries:
@@ -174,8 +175,20 @@ def _kv_transcript_from_captures(ctx: C.Context, wp: WeightProvider, x_attn_inpu
                                wv=[wp.weight(l, "Wv") for l in range(L)], scale_x=sx, n_kv_heads=cfg.n_kv_heads,
                                head_dim=cfg.d_head, per_tensor=per_tensor if per_tensor else None,
                                per_channel=per_channel, biases=biases, rope=rope)
-    k, v = C.kv_transcript(ctx, inp)
-    return k, v, [X, sx]
+    return inp, [X, sx]
+
+
+def _transcript_subset(inp: C.KvTranscriptInputs, layers: Sequence[int], n_pos: int) -> C.KvTranscriptInputs:
+    """The transcript inputs of ``layers`` over positions 0..n_pos-1 (the rows an opening reveals)."""
+    pick = lambda seq: None if seq is None else [seq[l] if l < len(seq) else None for l in layers]
+    xs = list(inp.x_attn)
+    sx = inp.scale_x
+    if sx is not None:
+        sx = sx[:n_pos][:, list(layers)].contiguous()
+    return C.KvTranscriptInputs(x_attn=[xs[l][:n_pos] for l in layers], wk=[inp.wk[l] for l in layers],
+                                wv=[inp.wv[l] for l in layers], scale_x=sx, n_kv_heads=inp.n_kv_heads,
+                                head_dim=inp.head_dim, per_tensor=pick(inp.per_tensor),
+                                per_channel=pick(inp.per_channel), biases=pick(inp.biases), rope=inp.rope)
 
 
 def _f32_host(x) -> np.ndarray:
@@ -231,6 +244,7 @@ class _Committed:
         self._kv_trees = kv_trees
         self._n_kv_layers = n_kv_layers
         self._kv_view = None
+        self._kvt = None                 # transcript inputs when the KV rows were recomputed and never stored
         self._host = None
 
     @property
@@ -320,21 +334,39 @@ class _Committed:
 
     # --- KV openings of open_v4 (prover/src/lib.rs:1564-1588) ---
     def kv_openings(self, token_index: int, layer_indices: Optional[Sequence[int]] = None):
-        """``(entries f64 [n_sel, t+1, 2, kv_dim], siblings uint8 [n_sel, t+1, depth, 32])`` on the host.
+        """``(layers, entries f64 [n_sel, t+1, 2, kv_dim], siblings uint8 [n_sel, t+1, depth, 32])`` on the host.
 
-        Entry [i][p] is the ``KvEntry`` of layer ``layer_indices[i]`` at position
-        p (``k_roped`` = [..., 0, :], ``v_deq`` = [..., 1, :]); the proof
+        Entry [i][p] is the ``KvEntry`` of layer ``layers[i]`` at position p
+        (``k_roped`` = [..., 0, :], ``v_deq`` = [..., 1, :]); the proof
         verifies ``hash_kv_entry(layer, p, k, v)`` against ``kv_roots[layer]``.
+        Rows the commit hashed without storing (the weight-provider path) are
+        recomputed here for the opened positions only.
         """
         if self._kv_trees is None:
             raise ValueError("no KV transcript was committed")
-        if not 0 <= token_index < self._kv_view.seq_lens[0]:
+        n_pos = self._kv_view.seq_lens[0] if self._kv_view is not None else self._n_kv_positions()
+        if not 0 <= token_index < n_pos:
             raise ValueError(f"token_index {token_index} out of range")
         layers = list(range(self._n_kv_layers)) if layer_indices is None else [int(l) for l in layer_indices]
         layers = [l for l in layers if 0 <= l < self._n_kv_layers]   # open_v4 skips unknown layers
-        ent, sib, _ = C.kv_open(self._ctx, self._kv_view, self._kv_trees, 0, layers, token_index + 1)
+        if self._kvt is None:
+            ent, sib, _ = C.kv_open(self._ctx, self._kv_view, self._kv_trees, 0, layers, token_index + 1)
+            self._ctx.sync()
+            return layers, ent.cpu().numpy(), sib.cpu().numpy()
+        if not layers:
+            return layers, np.zeros((0, token_index + 1, 2, 0)), np.zeros((0, token_index + 1, 0, 32), np.uint8)
+        with torch.cuda.stream(self._ctx.stream):
+            sub = _transcript_subset(self._kvt, layers, token_index + 1)
+        k, v = C.kv_transcript(self._ctx, sub)
+        n = token_index + 1
+        sib, depth = self._kv_trees.prove([l for l in layers for _ in range(n)], list(range(n)) * len(layers))
         self._ctx.sync()
-        return layers, ent.cpu().numpy(), sib.cpu().numpy()
+        ent = np.stack([k.cpu().numpy(), v.cpu().numpy()], axis=2)          # [n_sel, n, 2, kv]
+        return layers, ent, sib.cpu().numpy()[:, : depth[0]].reshape(len(layers), n, depth[0], 32)
+
+    def _n_kv_positions(self) -> int:
+        x = self._kvt.x_attn
+        return int((x[0] if not isinstance(x, torch.Tensor) else x[0]).shape[0])
 
     def audit_kv_json(self, token_index: int, layer_indices: Optional[Sequence[int]] = None) -> str:
         """The ``kv_entries`` / ``kv_proofs`` fields of ``V4AuditResponse`` in serde_json form
@@ -482,7 +514,7 @@ def _check_common(token_ids, sampling_seed, manifest):
 
 
 def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens, kv_cache, handle_cls,
-            manifest=None, **extra):
+            manifest=None, kvt: Optional[C.KvTranscriptInputs] = None, **extra):
     n = len(layout.tok_fwd)
     n_ids = token_ids.numel() if isinstance(token_ids, torch.Tensor) else len(token_ids)
     if n != n_ids:
@@ -502,6 +534,11 @@ def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens
         kv_trees.ctx = ctx               # later openings run on the main stream, after the join below
         kv_roots = r[0]
         n_kv_layers = len(kv_cache.k_layers)
+    elif kvt is not None:
+        side = ctx.fork()
+        kv_roots, kv_trees = C.kv_transcript_commit(side, kvt, keep_trees=True)
+        kv_trees.ctx = ctx
+        n_kv_layers = len(kvt.wk)
     # leaves and io values in one buffer so both trees build in one launch
     both = ctx.empty(2 * n, 32)
     C.trace_leaves(ctx, layout, out=both[:n])
@@ -525,6 +562,7 @@ def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens
     h = handle_cls(ctx, n, token_ids, n_prompt_tokens, digests, trees, kv_roots, kv_trees, n_kv_layers,
                    manifest=manifest, prompt=prompt, seed=seed, layout=layout, **extra)
     h._kv_view = kv_cache
+    h._kvt = kvt
     return h
 
 
@@ -602,16 +640,16 @@ def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_size
         if t is not None:
             lay.logits, lay.tok_logits_row = t, _wrap_rows(n_tok, rows, n_prompt_tokens, "logits")
             keep.append(t)
+    kvt = None
     if x_attn_inputs is not None and weight_provider is not None:
-        # the reference's path: K/V recomputed from x_attn + weights, then committed
+        # the reference's path: K/V recomputed from x_attn + weights and committed (one pass)
         if kv_cache is not None:
             raise ValueError("pass either kv_cache or x_attn_inputs with weight_provider, not both")
-        k, v, held = _kv_transcript_from_captures(ctx, weight_provider, x_attn_inputs, scales_d, fwd_batch_sizes,
-                                                  n_layers)
-        kv_cache = C.kv_transcript_view(k, v)
-        keep += [k, v] + held
+        kvt, held = _kv_transcript_from_captures(ctx, weight_provider, x_attn_inputs, scales_d, fwd_batch_sizes,
+                                                 n_layers)
+        keep += held
     h = _finish(ctx, lay, token_ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle,
-                manifest=man, x_attn=x_attn_inputs)
+                manifest=man, kvt=kvt, x_attn=x_attn_inputs)
     h._inputs = keep
     return h
 

@@ -363,6 +363,25 @@ typedef struct vc_kvt_desc {
  */
 VC_API vc_status vc_kv_transcript(vc_ctx* ctx, const vc_kvt_desc* desc, double* k_out_dev, double* v_out_dev);
 
+/*
+ * compute_kv_transcript and hot loop C of commit_minimal in one pass
+ * (crates/verilm-prover/src/lib.rs:207-329 then 449-482; the pair
+ * verilm-py/src/lib.rs:941-975 runs): per layer l, the kv_root of
+ * merkle::build_tree over hash_kv_entry(layer_base + l, p, K[l][p], V[l][p])
+ * for p in 0..n_tokens-1, with K/V exactly the f64 rows vc_kv_transcript
+ * writes.  The rows are hashed as they leave the tensor cores and never stored,
+ * so the kv_roots (and trees) equal vc_kv_transcript followed by vc_kv_commit
+ * (VC_DTYPE_F64) bit for bit, without the 16 bytes per K/V element pair of
+ * HBM traffic in between.  Openings re-derive the rows they reveal with
+ * vc_kv_transcript over the opened positions.
+ * kv_roots_dev: DEVICE [n_layers][32]; trees_out: optional, as for
+ * vc_kv_commit (tree index = l).  head_dim 64 or 128 with kv_dim a multiple of
+ * 128 run fused; other shapes run the two calls through device scratch.
+ * n_tokens >= 1.
+ */
+VC_API vc_status vc_kv_transcript_commit(vc_ctx* ctx, const vc_kvt_desc* desc, int32_t layer_base,
+                                         uint8_t* kv_roots_dev, vc_tree_set** trees_out);
+
 /* --------------------------------------------------------- measurement aid */
 
 /*

@@ -142,6 +142,20 @@ def _kv_transcript_from_captures(ctx: C.Context, wp: WeightProvider, x_attn_inpu
                 e += 1
             t0 += bs
         sx = scales_d.index_select(0, sx_idx.view(-1).to(dev)).view(n_tok, L)
+    return _kvt_token_major(ctx, wp, X, sx), [X, sx]
+
+
+def _kvt_token_major(ctx: C.Context, wp: WeightProvider, X: torch.Tensor, sx: torch.Tensor) -> C.KvTranscriptInputs:
+    """``compute_kv_transcript``'s inputs (prover/src/lib.rs:207-329) from x_attn
+    already token-major on the device: X int8 ``[n_tokens, layers, hidden]``,
+    sx float32 ``[n_tokens, layers]`` (each row's qkv_proj activation scale),
+    with the weights, scales, biases and RoPE of the weight provider."""
+    cfg = wp.config()
+    L = int(X.shape[1])
+    if L > cfg.n_layers:
+        raise ValueError(f"x_attn holds {L} layers, the model {cfg.n_layers}")
+    if int(X.shape[2]) != cfg.hidden_dim:
+        raise ValueError(f"x_attn rows hold {int(X.shape[2])} bytes, the model's hidden_dim is {cfg.hidden_dim}")
 
     def pair(seq, l, conv):
         if not seq or l >= len(seq) or seq[l] is None:
@@ -175,7 +189,7 @@ def _kv_transcript_from_captures(ctx: C.Context, wp: WeightProvider, x_attn_inpu
                                wv=[wp.weight(l, "Wv") for l in range(L)], scale_x=sx, n_kv_heads=cfg.n_kv_heads,
                                head_dim=cfg.d_head, per_tensor=per_tensor if per_tensor else None,
                                per_channel=per_channel, biases=biases, rope=rope)
-    return inp, [X, sx]
+    return inp
 
 
 def _transcript_subset(inp: C.KvTranscriptInputs, layers: Sequence[int], n_pos: int) -> C.KvTranscriptInputs:
@@ -712,6 +726,8 @@ def commit_minimal_packed(packed_a, packed_scales, n_layers, hidden_dim, fwd_bat
 def commit_request(a: torch.Tensor, scales_a: torch.Tensor, token_ids, prompt, sampling_seed, *,
                    n_prompt_tokens: Optional[int] = None, captured_logits_f32: Optional[torch.Tensor] = None,
                    kv_cache: Optional[C.KvCacheView] = None, manifest=None,
+                   x_attn: Optional[torch.Tensor] = None, scale_x_attn: Optional[torch.Tensor] = None,
+                   weight_provider: Optional[WeightProvider] = None,
                    ctx: Optional[C.Context] = None) -> MinimalBatchStateHandle:
     """One request's whole commitment, from captures already in device memory.
 
@@ -729,7 +745,10 @@ def commit_request(a: torch.Tensor, scales_a: torch.Tensor, token_ids, prompt, s
     host sequence or a 32-bit CUDA tensor); captured_logits_f32: float32
     ``[rows, vocab]``, row j bound to token ``gen_start + j`` with
     ``gen_start = n_prompt_tokens - 1`` (prover/src/lib.rs:367-390);
-    kv_cache: the request's K/V rows (one sequence).
+    kv_cache: the request's K/V rows (one sequence).  Or, as the reference
+    commits them, K/V recomputed from x_attn: int8 ``[n_tokens, layers,
+    hidden]`` (the qkv_proj input rows), scale_x_attn float32 ``[n_tokens,
+    layers]`` and a weight_provider (one pass, ``vc_kv_transcript_commit``).
     """
     ctx = ctx or C.Context()
     C._require_cuda(a, "a")
@@ -760,6 +779,21 @@ def commit_request(a: torch.Tensor, scales_a: torch.Tensor, token_ids, prompt, s
         lay.logits = lg
         lay.tok_logits_row = np.where((t >= 0) & (t < lg.shape[0]), t, -1).astype(np.int32)
         keep.append(lg)
-    h = _finish(ctx, lay, ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle, manifest=man)
+    kvt = None
+    if (x_attn is None) != (weight_provider is None) or (x_attn is None) != (scale_x_attn is None):
+        raise ValueError("x_attn, scale_x_attn and weight_provider go together")
+    if x_attn is not None:
+        if kv_cache is not None:
+            raise ValueError("pass either kv_cache or x_attn with weight_provider, not both")
+        C._require_cuda(x_attn, "x_attn")
+        C._require_cuda(scale_x_attn, "scale_x_attn")
+        if x_attn.dtype != torch.int8 or x_attn.dim() != 3 or int(x_attn.shape[0]) != n:
+            raise ValueError(f"x_attn must be an int8 [{n}, layers, hidden] CUDA tensor")
+        if scale_x_attn.dtype != torch.float32 or tuple(scale_x_attn.shape) != tuple(x_attn.shape[:2]):
+            raise ValueError(f"scale_x_attn must be a float32 [{n}, {int(x_attn.shape[1])}] CUDA tensor")
+        kvt = _kvt_token_major(ctx, weight_provider, x_attn, scale_x_attn.contiguous())
+        keep += [x_attn, scale_x_attn]
+    h = _finish(ctx, lay, ids, prompt, seed, n_prompt_tokens, kv_cache, MinimalBatchStateHandle, manifest=man,
+                kvt=kvt, x_attn=x_attn)
     h._inputs = keep
     return h

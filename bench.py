@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Trace-commitment throughput on B200 (trace bytes committed GB/s, + kv_roots/s).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5|c2|c2t|c3|c4|online|request] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5|c2|c2t|c3|c4|online|request|capture] [--impl ours|reference]
 
 A step is one pass of the commitment hot path over one batch of synthetic
 input already resident in HBM.
@@ -26,6 +26,11 @@ Whole-request workload:
   request  one c2-shaped request through verilm_rs.commit_minimal_from_captures: retained leaves with
       the captured-logits wrap, the IO chain, the trace/IO trees and the 32 KV trees of its cache,
       on overlapped streams.
+Capture workload:
+  capture  a batch-1 decode step of a Llama-3.1-8B-shaped stand-in model (bf16 weights; four
+      cutlass_scaled_mm-shaped calls per layer, lm_head, argmax sampler) with no capture, with the
+      device capture (commitllm_b200.capture), and with the reference's host-copy capture restated;
+      then each path's commit of the captured request.
 Except c5, every rank commits its own copy of the workload (weak scaling); at
 N > 1 the roots are all-gathered (NCCL) and the root-of-roots is built inside
 the step.
@@ -66,6 +71,10 @@ WORKLOADS = {
     # decode steps (4 096 committed tokens), captured logits for the 3 073 generated tokens, its KV cache
     "request": dict(kind="request", name="llama3.1-8b-request-4096", n_layers=32, hidden=4096, n_heads=8,
                     head_dim=128, n_seqs=1, seq_len=4096, n_prompt=1024, vocab=128256, x_attn=False, steps=20),
+    # capture cost per batch-1 decode step (Llama-3.1-8B shapes): no capture, the device capture, and the
+    # reference's host-copy capture; then each path's commit of the captured request
+    "capture": dict(kind="capture", name="llama3.1-8b-decode-capture", n_layers=32, hidden=4096, q_dim=4096,
+                    kv_dim=1024, intermediate=14336, vocab=128256, steps=64),
 }
 
 
@@ -933,6 +942,167 @@ def run_online(args, w, local):
     print(json.dumps(line), flush=True)
 
 
+class _HostCopyCapture:
+    """The reference's capture path restated for timing: each o_proj input
+    copied to a pinned host slab with a non-blocking device-to-host copy
+    (sidecar/verilm/capture.py:733-763), each qkv_proj input copied to the host
+    (x_attn capture, on by default at the server; capture.py:352-373, 930-933),
+    each call's scale kept as a GPU reference (capture.py:918-920), and each
+    sampled logits row pulled to the host with ``.float().cpu()``
+    (sampler.py:153-154).  The drain waits for the transfers and concatenates
+    the scales on the host."""
+
+    def __init__(self, n_layers, hidden, capacity_rows=32768):
+        import torch
+        self.L, self.H = n_layers, hidden
+        self.calls_per_fwd = 4 * n_layers
+        self.slab = torch.empty(capacity_rows, hidden, dtype=torch.int8, pin_memory=True)
+        self.reset()
+
+    def reset(self):
+        self.counter, self.idx = 0, 0
+        self.offsets, self.x_attn, self.scales, self.logits = [], [], [], []
+
+    def wrap(self, real):
+        def wrapped(a, b, scale_a, scale_b, out_dtype, bias=None):
+            out = real(a, b, scale_a, scale_b, out_dtype, bias)
+            proj = (self.counter % self.calls_per_fwd) % 4
+            self.counter += 1
+            self.scales.append(scale_a)
+            if proj == 1:
+                rows = a.shape[0]
+                self.slab[self.idx:self.idx + rows].copy_(a, non_blocking=True)
+                self.offsets.append((self.idx, self.idx + rows))
+                self.idx += rows
+            elif proj == 0:
+                self.x_attn.append(a.to("cpu", non_blocking=True))
+            return out
+        return wrapped
+
+    def capture_logits(self, logits):
+        self.logits.append(logits[-1].float().cpu().numpy())
+
+    def drain(self):
+        import torch
+        torch.cuda.synchronize()
+        o = [self.slab[s:e].numpy() for s, e in self.offsets]
+        sc = torch.cat([t.flatten() for t in self.scales]).cpu().numpy()
+        out = (o, sc, [t.numpy() for t in self.x_attn], self.logits)
+        self.reset()
+        return out
+
+
+def run_capture(args, w, local):
+    """Capture cost per batch-1 decode step, three ways, then each path's commit.
+
+    The stand-in model runs per layer the four cutlass_scaled_mm-shaped calls
+    (qkv_proj, o_proj, gate_up_proj, down_proj; bf16 weights of Llama-3.1-8B
+    shapes, int8 activation rows) through the op the capture wraps, then the
+    lm_head and an argmax sampler whose ``.item()`` ends the step (so a step's
+    wall time is its latency).  Arms: the bare op; the device capture
+    (DeviceCaptureBuffer + DeviceLogitsCapture); the reference's host-copy
+    capture restated (_HostCopyCapture).  Each captured request (warm-up and
+    timed steps) is then committed: the device captures in place
+    (commit_captures), the host copies through commit_minimal_from_captures."""
+    import numpy as np
+    import torch
+    from commitllm_b200 import capture as K
+    from commitllm_b200 import commit as C
+    from commitllm_b200 import verilm_rs as VR
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    L, H, I, V = w["n_layers"], w["hidden"], w["intermediate"], w["vocab"]
+    q = w["q_dim"] + 2 * w["kv_dim"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+    bf = torch.bfloat16
+    W = [[torch.randn(q, H, generator=g, device=dev, dtype=bf) * 0.02,
+          torch.randn(H, w["q_dim"], generator=g, device=dev, dtype=bf) * 0.02,
+          torch.randn(2 * I, H, generator=g, device=dev, dtype=bf) * 0.02,
+          torch.randn(H, I, generator=g, device=dev, dtype=bf) * 0.02] for _ in range(L)]
+    W_lm = torch.randn(V, H, generator=g, device=dev, dtype=bf) * 0.02
+    a_h = torch.randint(-128, 128, (1, H), generator=g, device=dev, dtype=torch.int8)
+    a_q = torch.randint(-128, 128, (1, w["q_dim"]), generator=g, device=dev, dtype=torch.int8)
+    a_i = torch.randint(-128, 128, (1, I), generator=g, device=dev, dtype=torch.int8)
+    s_row = torch.rand(1, 1, generator=g, device=dev) * 0.05 + 1e-3
+    h_last = torch.randn(1, H, generator=g, device=dev, dtype=bf)
+
+    def real(a, b, sa, sb, dt, bias=None):
+        return torch.matmul(a.to(bf), b.t())
+
+    def step(op, on_logits):
+        for l in range(L):
+            op(a_h, W[l][0], s_row, None, bf, None)
+            op(a_q, W[l][1], s_row, None, bf, None)
+            op(a_h, W[l][2], s_row, None, bf, None)
+            op(a_i, W[l][3], s_row, None, bf, None)
+        logits = torch.matmul(h_last, W_lm.t())
+        on_logits(logits)
+        return int(logits[-1].argmax().item())
+
+    dbuf = K.DeviceCaptureBuffer(L, H, o_dim=w["q_dim"], device=dev)
+    dlog = K.DeviceLogitsCapture(V, device=dev)
+    hcap = _HostCopyCapture(L, w["q_dim"])
+    arms = {"none": (real, lambda lg: None), "device": (dbuf.wrap(real), dlog.capture),
+            "host_copy": (hcap.wrap(real), hcap.capture_logits)}
+    n_req = args.warmup + args.steps
+    res = {}
+    with Clocks(local) as clk:
+        clk.mark_start()
+        for name, (op, on_logits) in arms.items():
+            for _ in range(args.warmup):
+                step(op, on_logits)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            walls = []
+            e0.record()
+            for _ in range(args.steps):
+                t0 = time.perf_counter()
+                step(op, on_logits)
+                walls.append(time.perf_counter() - t0)
+            e1.record()
+            torch.cuda.synchronize()
+            res[name] = {"ms_per_step": round(float(np.mean(walls)) * 1e3, 4),
+                         "median_ms": round(float(np.median(walls)) * 1e3, 4),
+                         "max_ms": round(float(np.max(walls)) * 1e3, 4),
+                         "device_ms_per_step": round(e0.elapsed_time(e1) / args.steps, 4)}
+        clk.mark_end()
+    ids = [int(t) for t in np.random.default_rng(3).integers(0, V, n_req + 1)]
+    ctx = C.Context(local)
+    prompt, seed = b"capture workload prompt", bytes(32)
+    commit_ms = {}
+    for rep in range(2):                      # the first commit of each path warms its plans
+        t0 = time.perf_counter()
+        caps, logits = (dbuf.drain(), dlog.drain()) if rep == 0 else (caps, logits)
+        hd = K.commit_captures(caps, ids[1:], prompt, seed, n_prompt_tokens=1, logits=logits, ctx=ctx)
+        root_d = hd.merkle_root_hex()
+        commit_ms["device"] = round((time.perf_counter() - t0) * 1e3, 3)
+        t0 = time.perf_counter()
+        if rep == 0:
+            o, sc, xs, lg = hcap.drain()
+        hh = VR.commit_minimal_from_captures(o, sc, L, [1] * n_req, ids[1:], prompt, seed, n_prompt_tokens=1,
+                                             captured_logits_f32=lg, ctx=ctx)
+        root_h = hh.merkle_root_hex()
+        commit_ms["host_copy"] = round((time.perf_counter() - t0) * 1e3, 3)
+    if root_d != root_h:
+        raise SystemExit("device and host-copy captures committed different roots")
+    d2h = L * (H + w["q_dim"]) + 4 * V + 4 * L * 4
+    ov = {k: round(res[k]["ms_per_step"] - res["none"]["ms_per_step"], 4) for k in ("device", "host_copy")}
+    line = {
+        "metric": "decode step with capture (ms)", "value": res["device"]["ms_per_step"], "unit": "ms",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["device"]["ms_per_step"],
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic",
+        "config": {"workload": w["name"], "n_layers": L, "hidden": H, "intermediate": I, "vocab": V, "batch": 1,
+                   "model": "stand-in: bf16 weights of Llama-3.1-8B shapes, random init"},
+        "arms": res, "capture_overhead_ms": ov,
+        "d2h_bytes_per_step": {"device": 0, "host_copy": d2h},
+        "commit_ms": dict(commit_ms, tokens=n_req, note="warm commit of the captured request (second of two)"),
+        "roots_equal": True, "clocks": clk.summary(), "e2e": None, "cpu_baseline": None, "roofline": None,
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def ctx_sm():
     import torch
     return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
@@ -1003,7 +1173,17 @@ def main():
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": "the reference has no online per-step commit"}))
             return
+        if w["kind"] == "capture":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the capture workload times the reference's "
+                                  "host-copy capture itself, in its own line"}))
+            return
         run_reference(args, w, rank, world)
+        return
+    if w["kind"] == "capture":
+        if world > 1:
+            raise SystemExit("the capture workload runs on one GPU")
+        run_capture(args, w, local)
         return
     if w["kind"] == "online":
         if world > 1:

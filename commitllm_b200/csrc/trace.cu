@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_
   const int32_t* tk = a.tok + 5 * int64_t(t);
   const int f = tk[0];
   const int64_t row = tk[1];
-  Sha256Stream<kTraceThreads, SPLIT> s;
+  Sha256Stream<kTraceThreads, SPLIT, SPLIT == 0 ? 2 : 1> s;
   s.opq = &a.opq;  // parameter space (__grid_constant__): read as constant operands
   s.init(sbuf + threadIdx.x);
   s.put_tag(kTagRetained, 14);

@@ -95,58 +95,154 @@ __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_
 //   prev = io_genesis_v4(prompt_hash)  = SHA256("vi-io-genesis-v4" || ph)
 //   io_t = io_hash_v4(leaf_t, tok_t, prev) = SHA256("vi-io-v4" || leaf || u32le tok || prev)
 // The 76-byte message is two blocks: [tag(2) leaf(8) tok(1) prev0..4] and
-// [prev5..7, 0x80000000, 0 x 11, 608].  The chain is serial, so each
-// sequence gets one thread on a warp of its own (its own scheduler slot); a
-// lone warp issues one integer-ALU instruction every other cycle, which sets
-// the per-token time (~3.5 us on B200).  Computing each token's first 11
-// rounds ahead in parallel, moving adds to the FMA pipe, or shortening the
-// round's dependency chain with extra adds were measured and did not help.
+// [prev5..7, 0x80000000, 0 x 11, 608].  The chain is serial, and a lone warp
+// issues at most one instruction every other cycle, so each sequence gets a
+// CTA of two warps that split every compression: warp 1 computes the message
+// schedules of both blocks (K[t] + W[t], t = 16..63) into shared memory in
+// 8-word chunks as soon as the previous chain value is known, and warp 0 runs
+// the rounds, taking each chunk as it is published (named barriers 2-7 for
+// block 1, 8-13 for block 2; barrier 1: warp 0 has published the chain
+// value).  Both warps walk the same tokens, and every barrier is executed by
+// whole warps (all lanes compute the same values, lane 0 stores them).
+// Measured as a microbenchmark: 2 364 instead of 3 201 cycles per chained
+// block; in this kernel, a 4 096-token chain: 15.5 -> 13.1 ms.
 // prev_io (optional): the chain continues from prev_io[s] instead of the
 // genesis, and the last value is written back there (online extension).
-__global__ void io_chain_kernel(int n_seqs, const int64_t* tok_off, const uint8_t* leaves,
-                                const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io,
-                                uint8_t* prev_io) {
-  const int s = blockIdx.x;   // one sequence per CTA of one warp; lane 0 runs the chain
-  if (s >= n_seqs || threadIdx.x != 0) return;
-  uint32_t prev[8];
-  if (prev_io) {
-    load_digest(prev_io + int64_t(s) * 32, prev);
-  } else {
-    uint32_t ph[8];
-    load_digest(prompt_hash + int64_t(s) * 32, ph);
-    uint32_t w[16] = {0x76692d69u, 0x6f2d6765u, 0x6e657369u, 0x732d7634u,  // "vi-io-genesis-v4"
-                      ph[0], ph[1], ph[2], ph[3], ph[4], ph[5], ph[6], ph[7],
-                      0x80000000u, 0u, 0u, 384u};
-    sha_init(prev);
-    compress(prev, w);
+constexpr int kIoBarPrev = 1, kIoBarS1 = 2, kIoBarS2 = 8, kIoThreads = 64;
+
+__device__ __forceinline__ void io_bar_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "n"(kIoThreads) : "memory");
+}
+__device__ __forceinline__ void io_bar_arrive(int id) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "n"(kIoThreads) : "memory");
+}
+
+// Rounds t .. t+7 with kw[t..t+7] = K[t] + W[t].
+#define VC_ROUNDS8(kw, t)                                  \
+  do {                                                     \
+    VC_SHA_ROUND(a, b, c, d, e, f, g, h, (kw)[(t) + 0]);  \
+    VC_SHA_ROUND(h, a, b, c, d, e, f, g, (kw)[(t) + 1]);  \
+    VC_SHA_ROUND(g, h, a, b, c, d, e, f, (kw)[(t) + 2]);  \
+    VC_SHA_ROUND(f, g, h, a, b, c, d, e, (kw)[(t) + 3]);  \
+    VC_SHA_ROUND(e, f, g, h, a, b, c, d, (kw)[(t) + 4]);  \
+    VC_SHA_ROUND(d, e, f, g, h, a, b, c, (kw)[(t) + 5]);  \
+    VC_SHA_ROUND(c, d, e, f, g, h, a, b, (kw)[(t) + 6]);  \
+    VC_SHA_ROUND(b, c, d, e, f, g, h, a, (kw)[(t) + 7]);  \
+  } while (0)
+
+// Warp 0's half of one compression: rounds 0-15 from the message words w,
+// rounds 16-63 from the schedule chunks warp 1 publishes at barriers bar0..bar0+5.
+__device__ __forceinline__ void io_rounds(uint32_t st[8], const uint32_t w[16], const uint32_t* kw, int bar0) {
+  uint32_t a = st[0], b = st[1], c = st[2], d = st[3], e = st[4], f = st[5], g = st[6], h = st[7];
+  uint32_t k0[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) k0[t] = c_K.v[t] + w[t];
+  VC_ROUNDS8(k0, 0);
+  VC_ROUNDS8(k0, 8);
+#pragma unroll
+  for (int ch = 0; ch < 6; ++ch) {
+    io_bar_sync(bar0 + ch);
+    VC_ROUNDS8(kw, 16 + 8 * ch);
   }
+  st[0] += a; st[1] += b; st[2] += c; st[3] += d;
+  st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+}
+
+// Warp 1's half: the schedule of message w, K + W of rounds 16-63 into kw, one
+// barrier arrival per 8 words.
+__device__ __forceinline__ void io_schedule(uint32_t w[16], uint32_t* kw, int bar0, bool store) {
+#pragma unroll
+  for (int ch = 0; ch < 6; ++ch) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int t = 16 + 8 * ch + q;
+      const int j = t & 15;
+      w[j] += sig1(w[(j + 14) & 15]) + w[(j + 9) & 15] + sig0(w[(j + 1) & 15]);
+      if (store) kw[t] = c_K.v[t] + w[j];
+    }
+    __syncwarp();
+    io_bar_arrive(bar0 + ch);
+  }
+}
+
+__global__ void __launch_bounds__(kIoThreads) io_chain_kernel(int n_seqs, const int64_t* tok_off,
+                                                              const uint8_t* leaves, const uint32_t* token_ids,
+                                                              const uint8_t* prompt_hash, uint8_t* io,
+                                                              uint8_t* prev_io) {
+  __shared__ uint32_t kw1[64], kw2[64];   // K + W of each block's rounds 16-63
+  __shared__ uint32_t sprev[8];           // the chain value the current token extends
+  const int s = blockIdx.x;
+  if (s >= n_seqs) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t0 = tok_off[s], t1 = tok_off[s + 1];
   if (t0 >= t1) return;   // nothing appended: prev_io keeps its value
   uint32_t leaf[8], tok;
   load_digest(leaves + t0 * 32, leaf);
   tok = token_ids[t0];
-  for (int64_t t = t0; t < t1; ++t) {
-    // the next token's inputs do not depend on the chain: fetch them now
-    uint32_t nleaf[8], ntok = 0;
-    if (t + 1 < t1) {
-      load_digest(leaves + (t + 1) * 32, nleaf);
-      ntok = token_ids[t + 1];
+  if (warp == 0) {
+    uint32_t prev[8];
+    if (prev_io) {
+      load_digest(prev_io + int64_t(s) * 32, prev);
+    } else {
+      uint32_t ph[8];
+      load_digest(prompt_hash + int64_t(s) * 32, ph);
+      uint32_t w[16] = {0x76692d69u, 0x6f2d6765u, 0x6e657369u, 0x732d7634u,  // "vi-io-genesis-v4"
+                        ph[0], ph[1], ph[2], ph[3], ph[4], ph[5], ph[6], ph[7],
+                        0x80000000u, 0u, 0u, 384u};
+      sha_init(prev);
+      compress(prev, w);
     }
-    uint32_t w[16] = {0x76692d69u, 0x6f2d7634u,  // "vi-io-v4"
-                      leaf[0], leaf[1], leaf[2], leaf[3], leaf[4], leaf[5], leaf[6], leaf[7],
-                      bswap32(tok), prev[0], prev[1], prev[2], prev[3], prev[4]};
-    uint32_t st[8];
-    sha_init(st);
-    compress(st, w);
-    uint32_t w2[16] = {prev[5], prev[6], prev[7], 0x80000000u, 0u, 0u, 0u, 0u,
-                       0u, 0u, 0u, 0u, 0u, 0u, 0u, 608u};
-    compress(st, w2);
-    store_digest(io + t * 32, st);
+    for (int64_t t = t0; t < t1; ++t) {
+      if (lane == 0) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) { prev[i] = st[i]; leaf[i] = nleaf[i]; }
-    tok = ntok;
+        for (int i = 0; i < 8; ++i) sprev[i] = prev[i];
+      }
+      __syncwarp();
+      io_bar_arrive(kIoBarPrev);
+      // the next token's inputs do not depend on the chain: fetch them now
+      uint32_t nleaf[8], ntok = 0;
+      if (t + 1 < t1) {
+        load_digest(leaves + (t + 1) * 32, nleaf);
+        ntok = token_ids[t + 1];
+      }
+      const uint32_t w1[16] = {0x76692d69u, 0x6f2d7634u,  // "vi-io-v4"
+                               leaf[0], leaf[1], leaf[2], leaf[3], leaf[4], leaf[5], leaf[6], leaf[7],
+                               bswap32(tok), prev[0], prev[1], prev[2], prev[3], prev[4]};
+      uint32_t st[8];
+      sha_init(st);
+      io_rounds(st, w1, kw1, kIoBarS1);
+      const uint32_t w2[16] = {prev[5], prev[6], prev[7], 0x80000000u, 0u, 0u, 0u, 0u,
+                               0u, 0u, 0u, 0u, 0u, 0u, 0u, 608u};
+      io_rounds(st, w2, kw2, kIoBarS2);
+      if (lane == 0) store_digest(io + t * 32, st);
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { prev[i] = st[i]; leaf[i] = nleaf[i]; }
+      tok = ntok;
+    }
+    if (prev_io && lane == 0) store_digest(prev_io + int64_t(s) * 32, prev);
+  } else {
+    for (int64_t t = t0; t < t1; ++t) {
+      uint32_t nleaf[8], ntok = 0;
+      if (t + 1 < t1) {
+        load_digest(leaves + (t + 1) * 32, nleaf);
+        ntok = token_ids[t + 1];
+      }
+      io_bar_sync(kIoBarPrev);
+      uint32_t p[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) p[i] = sprev[i];
+      uint32_t w1[16] = {0x76692d69u, 0x6f2d7634u,
+                         leaf[0], leaf[1], leaf[2], leaf[3], leaf[4], leaf[5], leaf[6], leaf[7],
+                         bswap32(tok), p[0], p[1], p[2], p[3], p[4]};
+      io_schedule(w1, kw1, kIoBarS1, lane == 0);
+      uint32_t w2[16] = {p[5], p[6], p[7], 0x80000000u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 608u};
+      io_schedule(w2, kw2, kIoBarS2, lane == 0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) leaf[i] = nleaf[i];
+      tok = ntok;
+    }
   }
-  if (prev_io) store_digest(prev_io + int64_t(s) * 32, prev);
 }
 
 // SHA256(tag || data_i), one thread per message.  tag 0: "vi-prompt-v1"
@@ -185,7 +281,8 @@ cudaError_t launch_trace_leaves(const TraceArgs& a, int n_sm, cudaStream_t s) {
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,
                             const uint32_t* token_ids, const uint8_t* prompt_hash, uint8_t* io, uint8_t* prev_io,
                             cudaStream_t s) {
-  io_chain_kernel<<<n_seqs, 32, 0, s>>>(n_seqs, tok_off_dev, leaves, token_ids, prompt_hash, io, prev_io);
+  if (n_seqs == 0) return cudaSuccess;
+  io_chain_kernel<<<n_seqs, kIoThreads, 0, s>>>(n_seqs, tok_off_dev, leaves, token_ids, prompt_hash, io, prev_io);
   return cudaGetLastError();
 }
 

@@ -762,6 +762,7 @@ vc_status vc_trace_leaves(vc_ctx* c, const vc_trace_desc* d, uint8_t* leaves_dev
   a.vocab = d->vocab;
   a.logits_stride = d->logits_stride;
   a.leaves = leaves_dev;
+  a.err = c->err;
   if (reinterpret_cast<uintptr_t>(leaves_dev) % 16) return fail(VC_EINVAL, "vc_trace_leaves: leaves_dev not 16-byte aligned");
   const cudaError_t e = launch_trace_leaves(a, c->n_sm, c->stream);
   if (e != cudaSuccess) return fail(VC_ECUDA, "vc_trace_leaves launch: %s", cudaGetErrorString(e));

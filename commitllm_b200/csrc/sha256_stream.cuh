@@ -10,6 +10,8 @@
 // All threads of a warp hash messages of the same layout, so the fill
 // position -- and every branch on it -- is warp-uniform.
 #pragma once
+#include <type_traits>
+
 #include "sha256_bal.cuh"
 #include "sha256_core.cuh"
 
@@ -22,10 +24,14 @@ namespace vc {
 // request: trace leaves 25.5 -> 23.5 ms); with many threads per SM the
 // second 17-word buffer costs more in registers than it hides (C4: 129.8 ->
 // 144.2 ms), so the busy configurations keep one.
-template <int NT, int BAL = 0, int PF = 1>
+// Sink: when not void, every completed 64-byte block goes to sink->push(w)
+// instead of into this stream's own compression (h is then unused): the
+// producer half of a split compression.
+template <int NT, int BAL = 0, int PF = 1, class Sink = void>
 struct Sha256Stream {
   uint32_t h[8];
   const Opq* opq = nullptr;
+  Sink* sink = nullptr;
   uint32_t* buf;    // this thread's column of the CTA's [16][NT] buffer
   uint32_t fill;    // bytes of the current block, pending partial word included (0..63)
   uint32_t carry;   // the fill % 4 pending bytes, left-aligned big-endian
@@ -40,7 +46,9 @@ struct Sha256Stream {
   }
 
   __device__ __forceinline__ void cmp(uint32_t w[16]) {
-    if constexpr (BAL == 0)
+    if constexpr (!std::is_void_v<Sink>)
+      sink->push(w);
+    else if constexpr (BAL == 0)
       compress(h, w);
     else
       compress_bal<BAL>(h, w, *opq);

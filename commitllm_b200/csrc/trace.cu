@@ -1,6 +1,7 @@
 // Retained-state ("trace") leaves, the IO hash chain, and small tagged hashes.
 #include "sha256_core.cuh"
 #include "sha256_stream.cuh"
+#include "tc05.cuh"
 #include "vc_internal.h"
 
 namespace vc {
@@ -89,6 +90,194 @@ __global__ void __launch_bounds__(kTraceThreads) trace_leaf_kernel(const __grid_
     for (int w = 0; w < 8; ++w) d[w] = s.h[w];
   }
   store_digest(a.leaves + int64_t(t) * 32, d);
+}
+
+// The same leaves when few tokens are hashed (a request or a decode step):
+// each of them is one long serial chain (10 068 blocks for a Llama-8B token
+// with its logits), so time is one thread's latency per block, and a lone
+// warp issues at most one instruction every other cycle.  A CTA of two warps
+// splits each compression: lane l of warp 1 walks token l's message (the
+// same field streaming as trace_leaf_kernel) and, for every block, writes
+// K[t] + W[t] of all 64 rounds (message schedule included) into a 4-slot ring
+// in shared memory; lane l of warp 0 runs the rounds of token l from it.
+// Each lane has its own mbarriers (full / empty per slot, count 1), so lanes
+// move independently and no barrier depends on the warp being converged; a
+// wrap message starts with the previous digest, which warp 0 hands back
+// through shared memory and a third per-lane mbarrier.  Every wait gives up
+// after 1 s of %globaltimer and sets the context's error flag to 2.
+constexpr int kSplitSlots = 4;
+constexpr int kSplitLanes = 32;
+constexpr uint64_t kSplitWaitNs = 1000000000ull;
+// at most this many two-warp CTAs per SM; above it the one-thread kernel's
+// throughput wins
+constexpr int kSplitMaxPairsPerSm = 2;
+
+struct SplitSmem {
+  uint4 kw[kSplitSlots][16][kSplitLanes];   // K + W of a block: [slot][rounds / 4][lane], 4 rounds per uint4
+  uint32_t dig[8][kSplitLanes];             // digest handed from warp 0 to warp 1
+  uint32_t sbuf[16 * kSplitLanes];          // warp 1's block buffer (Sha256Stream)
+  uint64_t full[kSplitSlots][kSplitLanes];
+  uint64_t empty[kSplitSlots][kSplitLanes];
+  uint64_t dready[kSplitLanes];
+};
+
+// Warp 1's sink: the schedule of each completed block into the lane's ring.
+struct KwSink {
+  SplitSmem* sm;
+  int* err;
+  uint32_t lane;
+  uint32_t k;     // blocks pushed
+  bool ok;
+  __device__ __forceinline__ void push(uint32_t w[16]) {
+    if (!ok) return;
+    const uint32_t slot = k % kSplitSlots, u = k / kSplitSlots;
+    if (u > 0 && !tc05::mbar_wait(tc05::smem_u32(&sm->empty[slot][lane]), (u - 1) & 1u, kSplitWaitNs)) {
+      atomicExch(err, 2);
+      ok = false;
+      return;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      sm->kw[slot][q][lane] = make_uint4(c_K.v[4 * q] + w[4 * q], c_K.v[4 * q + 1] + w[4 * q + 1],
+                                         c_K.v[4 * q + 2] + w[4 * q + 2], c_K.v[4 * q + 3] + w[4 * q + 3]);
+#pragma unroll
+    for (int q = 4; q < 16; ++q) {
+      uint32_t v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int t = 4 * q + i, j = t & 15;
+        w[j] += sig1(w[(j + 14) & 15]) + w[(j + 9) & 15] + sig0(w[(j + 1) & 15]);
+        v[i] = c_K.v[t] + w[j];
+      }
+      sm->kw[slot][q][lane] = make_uint4(v[0], v[1], v[2], v[3]);
+    }
+    tc05::mbar_arrive(tc05::smem_u32(&sm->full[slot][lane]));
+    ++k;
+  }
+};
+
+__device__ __forceinline__ int64_t sha_blocks_of(int64_t len) { return (len + 9 + 63) / 64; }
+
+__global__ void __launch_bounds__(2 * kSplitLanes) trace_leaf_split_kernel(const __grid_constant__ TraceArgs a) {
+  __shared__ SplitSmem sm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kSplitLanes + lane;
+  if (warp == 0) {
+    for (int sl = 0; sl < kSplitSlots; ++sl) {
+      tc05::mbar_init(tc05::smem_u32(&sm.full[sl][lane]), 1);
+      tc05::mbar_init(tc05::smem_u32(&sm.empty[sl][lane]), 1);
+    }
+    tc05::mbar_init(tc05::smem_u32(&sm.dready[lane]), 1);
+  }
+  __syncthreads();
+  if (t >= a.n_tokens) return;    // per lane: this lane's token does not exist, and its pair skips it too
+  const int32_t* tk = a.tok + 5 * int64_t(t);
+  // the lane's messages: the retained state, then the wraps it has, in order
+  const int64_t len0 = 14 + int64_t(a.n_layers) * (a.hidden + 5 + (a.x_rows ? a.hidden + 4 : 0));
+  const bool has[3] = {tk[2] >= 0, tk[3] >= 0, tk[4] >= 0};
+  const int64_t wlen[3] = {17 + 32 + int64_t(a.fr_dim) * 4, 17 + 32 + int64_t(a.lp_dim) * 2,
+                           21 + 32 + int64_t(a.vocab) * 4};
+  const int n_wraps = int(has[0]) + int(has[1]) + int(has[2]);
+  if (warp == 0) {
+    // ------------------------------------------------------------------ rounds
+    uint32_t k = 0, handed = 0;
+    uint32_t d[8];
+    bool ok = true;
+    for (int m = 0; m < 4 && ok; ++m) {
+      if (m > 0 && !has[m - 1]) continue;
+      const int64_t nb = sha_blocks_of(m == 0 ? len0 : wlen[m - 1]);
+      uint32_t st[8];
+      sha_init(st);
+      for (int64_t b = 0; b < nb; ++b, ++k) {
+        const uint32_t slot = k % kSplitSlots, u = k / kSplitSlots;
+        if (!tc05::mbar_wait(tc05::smem_u32(&sm.full[slot][lane]), u & 1u, kSplitWaitNs)) {
+          atomicExch(a.err, 2);
+          ok = false;
+          break;
+        }
+        uint4 kv[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) kv[q] = sm.kw[slot][q][lane];
+        tc05::mbar_arrive(tc05::smem_u32(&sm.empty[slot][lane]));
+        const uint32_t* kw = reinterpret_cast<const uint32_t*>(kv);
+        uint32_t a_ = st[0], b_ = st[1], c_ = st[2], d_ = st[3], e_ = st[4], f_ = st[5], g_ = st[6], h_ = st[7];
+#pragma unroll
+        for (int r = 0; r < 64; r += 8) {
+          VC_SHA_ROUND(a_, b_, c_, d_, e_, f_, g_, h_, kw[r + 0]);
+          VC_SHA_ROUND(h_, a_, b_, c_, d_, e_, f_, g_, kw[r + 1]);
+          VC_SHA_ROUND(g_, h_, a_, b_, c_, d_, e_, f_, kw[r + 2]);
+          VC_SHA_ROUND(f_, g_, h_, a_, b_, c_, d_, e_, kw[r + 3]);
+          VC_SHA_ROUND(e_, f_, g_, h_, a_, b_, c_, d_, kw[r + 4]);
+          VC_SHA_ROUND(d_, e_, f_, g_, h_, a_, b_, c_, kw[r + 5]);
+          VC_SHA_ROUND(c_, d_, e_, f_, g_, h_, a_, b_, kw[r + 6]);
+          VC_SHA_ROUND(b_, c_, d_, e_, f_, g_, h_, a_, kw[r + 7]);
+        }
+        st[0] += a_; st[1] += b_; st[2] += c_; st[3] += d_;
+        st[4] += e_; st[5] += f_; st[6] += g_; st[7] += h_;
+      }
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = st[w];
+      if (ok && int(handed) < n_wraps) {
+        // the next message of this lane starts with this digest
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sm.dig[w][lane] = d[w];
+        tc05::mbar_arrive(tc05::smem_u32(&sm.dready[lane]));
+        ++handed;
+      }
+    }
+    if (ok) store_digest(a.leaves + int64_t(t) * 32, d);
+  } else {
+    // ------------------------------------------------------ message + schedule
+    KwSink sink{&sm, a.err, uint32_t(lane), 0u, true};
+    Sha256Stream<kSplitLanes, 0, 2, KwSink> s;
+    s.sink = &sink;
+    const int f = tk[0];
+    const int64_t row = tk[1];
+    s.init(sm.sbuf + lane);
+    s.put_tag(kTagRetained, 14);
+    for (int l = 0; l < a.n_layers; ++l) {
+      const int64_t fl = int64_t(f) * a.n_layers + l;
+      const uint8_t* arow = static_cast<const uint8_t*>(a.a_rows[fl]) + row * a.hidden;
+      s.put_array(arow, a.hidden);
+      s.put_le(__ldg(static_cast<const uint32_t*>(a.scale_a[fl]) + row * a.scale_stride));
+      if (a.x_rows) {
+        s.put_byte(1);
+        const uint8_t* xrow = static_cast<const uint8_t*>(a.x_rows[fl]) + row * a.hidden;
+        s.put_array(xrow, a.hidden);
+        s.put_le(__ldg(static_cast<const uint32_t*>(a.scale_x[fl]) + row * a.scale_x_stride));
+      } else {
+        s.put_byte(0);
+      }
+    }
+    s.finish();
+    uint32_t waited = 0;
+    for (int wi = 0; wi < 3 && sink.ok; ++wi) {
+      if (!has[wi]) continue;
+      if (!tc05::mbar_wait(tc05::smem_u32(&sm.dready[lane]), waited & 1u, kSplitWaitNs)) {
+        atomicExch(a.err, 2);
+        break;
+      }
+      ++waited;
+      uint32_t d[8];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) d[w] = sm.dig[w][lane];
+      s.init(sm.sbuf + lane);
+      if (wi == 0) {
+        s.put_tag(kTagFr, 17);
+        s.put_digest(d);
+        s.put_array(a.fr + int64_t(tk[2]) * a.fr_stride * 4, int64_t(a.fr_dim) * 4);
+      } else if (wi == 1) {
+        s.put_tag(kTagLp, 17);
+        s.put_digest(d);
+        s.put_array(a.lp + int64_t(tk[3]) * a.lp_stride * 2, int64_t(a.lp_dim) * 2);
+      } else {
+        s.put_tag(kTagLogits, 21);
+        s.put_digest(d);
+        s.put_array(a.logits + int64_t(tk[4]) * a.logits_stride * 4, int64_t(a.vocab) * 4);
+      }
+      s.finish();
+    }
+  }
 }
 
 // IO chain (prover/src/lib.rs:403-410):
@@ -271,8 +460,11 @@ __global__ void __launch_bounds__(kTraceThreads) tagged_hash_kernel(int n, int t
 cudaError_t launch_trace_leaves(const TraceArgs& a, int n_sm, cudaStream_t s) {
   if (a.n_tokens == 0) return cudaSuccess;
   const int grid = (a.n_tokens + kTraceThreads - 1) / kTraceThreads;
+  const int pairs = (a.n_tokens + kSplitLanes - 1) / kSplitLanes;
   if (grid >= kTraceSplitMinCtasPerSm * n_sm)
     trace_leaf_kernel<kTraceSplit><<<grid, kTraceThreads, 0, s>>>(a);
+  else if (pairs <= kSplitMaxPairsPerSm * n_sm)
+    trace_leaf_split_kernel<<<pairs, 2 * kSplitLanes, 0, s>>>(a);
   else
     trace_leaf_kernel<0><<<grid, kTraceThreads, 0, s>>>(a);
   return cudaGetLastError();

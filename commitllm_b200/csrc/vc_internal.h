@@ -103,6 +103,7 @@ struct TraceArgs {
   const uint8_t* logits; int32_t vocab; int64_t logits_stride;
   uint8_t* leaves;
   Opq opq;                      // multipliers of the balanced compression (make_opq())
+  int* err;                     // the context's error flag (2: a bounded wait ran out)
 };
 cudaError_t launch_trace_leaves(const TraceArgs& a, int n_sm, cudaStream_t s);
 cudaError_t launch_io_chain(int n_seqs, const int64_t* tok_off_dev, const uint8_t* leaves,

@@ -538,24 +538,31 @@ def _finish(ctx, layout: C.TraceLayout, token_ids, prompt, seed, n_prompt_tokens
     kv_roots = kv_trees = None
     n_kv_layers = 0
     side = None
-    if kv_cache is not None:
-        if len(kv_cache.seq_lens) != 1:
-            raise ValueError("kv_cache must describe exactly the request's one sequence")
-        # the KV trees run on a second stream, beside the trace leaves and the IO chain:
-        # for one request those are a few thousand serial SHA chains on a few SMs
+    if kv_cache is not None and len(kv_cache.seq_lens) != 1:
+        raise ValueError("kv_cache must describe exactly the request's one sequence")
+    # The KV trees run on a second stream, beside the trace leaves and the IO
+    # chain: for one request those are a few thousand serial SHA chains on one
+    # SM each.  The side stream waits only for the work queued before the fork.
+    if kv_cache is not None or kvt is not None:
         side = ctx.fork()
-        r, kv_trees = C.kv_commit(side, kv_cache, keep_trees=True)
-        kv_trees.ctx = ctx               # later openings run on the main stream, after the join below
-        kv_roots = r[0]
-        n_kv_layers = len(kv_cache.k_layers)
-    elif kvt is not None:
-        side = ctx.fork()
+    if kvt is not None:
+        # the one-pass transcript kernel holds whole SMs (one persistent CTA each):
+        # it goes first, and the trace leaves start on the SMs it leaves
         kv_roots, kv_trees = C.kv_transcript_commit(side, kvt, keep_trees=True)
-        kv_trees.ctx = ctx
+        kv_trees.ctx = ctx               # later openings run on the main stream, after the join below
         n_kv_layers = len(kvt.wk)
     # leaves and io values in one buffer so both trees build in one launch
     both = ctx.empty(2 * n, 32)
     C.trace_leaves(ctx, layout, out=both[:n])
+    if kv_cache is not None:
+        # launched after the trace leaves, so that their latency-bound CTAs are
+        # placed one per SM before the KV kernel's CTAs fill the GPU (placed after
+        # them, several trace CTAs shared SMs and the request took 36 instead of
+        # 18 ms of trace leaves)
+        r, kv_trees = C.kv_commit(side, kv_cache, keep_trees=True)
+        kv_trees.ctx = ctx
+        kv_roots = r[0]
+        n_kv_layers = len(kv_cache.k_layers)
     if isinstance(token_ids, torch.Tensor) and token_ids.is_cuda:
         if token_ids.dtype not in (torch.int32, torch.uint32) or token_ids.numel() != n:
             raise ValueError("token_ids on the device must be a 32-bit tensor of n_tokens entries")

@@ -21,7 +21,7 @@ SYMBOLS = (
     "vc_abi_version", "vc_last_error", "vc_ctx_create", "vc_ctx_destroy", "vc_ctx_sync",
     "vc_kv_commit", "vc_trace_leaves", "vc_io_chain", "vc_prompt_hash", "vc_seed_commitment",
     "vc_build_trees", "vc_prove", "vc_tree_set_count", "vc_tree_nodes", "vc_tree_set_free",
-    "vc_int_peak", "vc_kv_commit_noalloc", "vc_kv_open", "vc_io_extend", "vc_io_genesis",
+    "vc_int_peak", "vc_wait_probe", "vc_kv_commit_noalloc", "vc_kv_open", "vc_io_extend", "vc_io_genesis",
     "vc_kv_transcript", "vc_kv_transcript_commit",
 )
 
@@ -107,6 +107,7 @@ def _declare(lib):
         "vc_tree_nodes": [P, c_int32, POINTER(P), POINTER(c_int64), POINTER(c_int64)],
         "vc_tree_set_free": [P],
         "vc_int_peak": [P, c_int32, c_int64, POINTER(c_double)],
+        "vc_wait_probe": [P, c_int64],
         "vc_kv_commit_noalloc": [POINTER(KvDesc), P, P, P],
         "vc_kv_open": [P, POINTER(KvDesc), P, c_int32, c_int32, POINTER(c_int32), c_int32, P, P, c_int32,
                        POINTER(c_int32)],

@@ -563,6 +563,13 @@ def int_peak(ctx: Context, variant: int = 0, iters: int = 20000) -> float:
     return v.value
 
 
+def wait_probe(ctx: Context, limit_ns: int) -> None:
+    """Queue the bounded-wait probe (``vc_wait_probe``): a wait that nothing
+    satisfies gives up after ``limit_ns`` and flags the context, so the next
+    :meth:`Context.sync` raises the timeout and the context stays usable."""
+    check(lib().vc_wait_probe(ctx.handle, int(limit_ns)))
+
+
 # --------------------------------------------------------------------------
 # KV transcript: compute_kv_transcript (crates/verilm-prover/src/lib.rs:207-329)
 # --------------------------------------------------------------------------

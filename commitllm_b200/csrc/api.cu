@@ -1087,4 +1087,12 @@ vc_status vc_int_peak(vc_ctx* c, int32_t variant, int64_t iters, double* ops_per
   return VC_OK;
 }
 
+vc_status vc_wait_probe(vc_ctx* c, int64_t limit_ns) {
+  if (!c || limit_ns < 1 || limit_ns > 2000000000) return fail(VC_EINVAL, "vc_wait_probe: limit_ns must be in [1, 2e9]");
+  DeviceGuard g(c->device);
+  const cudaError_t e = launch_wait_probe(uint64_t(limit_ns), c->err, c->stream);
+  if (e != cudaSuccess) return fail(VC_ECUDA, "vc_wait_probe launch: %s", cudaGetErrorString(e));
+  return VC_OK;
+}
+
 }  // extern "C"

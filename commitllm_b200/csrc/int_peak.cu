@@ -4,6 +4,8 @@
 // compression round's operation counts (6 rotates, 4 LOP3, 4 adds): the
 // denominator of the hash roofline.
 #include <cstdint>
+
+#include "tc05.cuh"
 #include "vc_internal.h"
 
 namespace vc {
@@ -91,6 +93,22 @@ cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink
     default: int_peak_kernel<3><<<blocks, kPeakThreads, 0, s>>>(iters, 6u, sink); break;
   }
   *ops_per_launch = double(blocks) * kPeakThreads * double(iters) * kChains * 14.0;
+  return cudaGetLastError();
+}
+
+// The library's bounded wait with nothing to wait for: one thread waits on an
+// mbarrier that no thread arrives at.  The wait gives up after limit_ns of
+// %globaltimer and sets the context's error flag to 2, as every bounded wait of
+// the commit kernels does; the kernel then returns normally.
+__global__ void wait_probe_kernel(uint64_t limit_ns, int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) tc05::mbar_init(tc05::smem_u32(&bar), 1);
+  __syncthreads();
+  if (threadIdx.x == 0 && !tc05::mbar_wait(tc05::smem_u32(&bar), 0, limit_ns)) atomicExch(err, 2);
+}
+
+cudaError_t launch_wait_probe(uint64_t limit_ns, int* err, cudaStream_t s) {
+  wait_probe_kernel<<<1, 32, 0, s>>>(limit_ns, err);
   return cudaGetLastError();
 }
 

@@ -162,5 +162,6 @@ cudaError_t launch_kvt_commit(const KvtcArgs& a, int n_sm, cudaStream_t s);
 // int_peak.cu
 cudaError_t launch_int_peak(int variant, int64_t iters, int n_sm, uint32_t* sink, cudaStream_t s,
                             double* ops_per_launch);
+cudaError_t launch_wait_probe(uint64_t limit_ns, int* err, cudaStream_t s);
 
 }  // namespace vc

@@ -393,6 +393,17 @@ VC_API vc_status vc_kv_transcript_commit(vc_ctx* ctx, const vc_kvt_desc* desc, i
  */
 VC_API vc_status vc_int_peak(vc_ctx* ctx, int32_t variant, int64_t iters, double* ops_per_s);
 
+/*
+ * Bounded-wait probe (no reference counterpart; the reference has no device
+ * waits): launches one thread that waits on an mbarrier nothing arrives at.
+ * Its wait gives up after limit_ns (1 .. 2e9) nanoseconds and sets the
+ * context's error flag, exactly as a bounded wait of the commit kernels does
+ * when the work it waits for never lands; the next vc_ctx_sync then returns
+ * VC_ETIMEDOUT and clears the flag, and the context stays usable.  Lets a
+ * caller check that failure path without faulting or hanging a GPU.
+ */
+VC_API vc_status vc_wait_probe(vc_ctx* ctx, int64_t limit_ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -755,6 +755,20 @@ def cpu_kvt(w, n_pos, n_threads, seed=11):
     return time.perf_counter() - t0
 
 
+def cpu_host():
+    """The host CPU the CPU legs ran on: model name and hardware threads."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "host_threads": os.cpu_count() or 1}
+
+
 def cpu_leg(w, reference_threads: bool, budget_s: float = 20.0, reps: int = 1):
     """(GB/s, threads, sample text, seconds) of the CPU restatement on a bounded sample of w."""
     ncpu = os.cpu_count() or 1
@@ -1132,7 +1146,7 @@ def run_reference(args, w, rank, world):
         "scaling": "strong" if (w.get("job") or args.split_trees) else "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic", "config": config_of(dict(w, split=world) if args.split_trees else w, world),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample + f", median of {reps} steps"},
+                         "sample": sample + f", median of {reps} steps", **cpu_host()},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -1443,7 +1457,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         val, cores, sample, dt = cpu_leg(w, reference_threads=True)
         cpu = {"value": round(val, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": sample + f" ({dt:.2f} s); the reference's own threading for this path"}
+               "sample": sample + f" ({dt:.2f} s); the reference's own threading for this path", **cpu_host()}
 
     if world > 1:
         dist.destroy_process_group()

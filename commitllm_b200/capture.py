@@ -37,7 +37,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass
-from typing import Callable, List, Optional
+from typing import Callable, List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -180,6 +180,7 @@ class DeviceCaptureBuffer:
         self.total_captured = 0
         self._counter = 0
         self._installed = None
+        self.before_grow: Optional[Callable[[], None]] = None
         self._request_id: Optional[str] = None
         self._prompt_ids: List[int] = []
         self._request_start = 0.0
@@ -220,6 +221,8 @@ class DeviceCaptureBuffer:
     def _reserve(self, rows: int) -> None:
         if self._a is not None and rows <= self._a.shape[0]:
             return
+        if self._a is not None and self.before_grow is not None:
+            self.before_grow()          # work that addresses the current slabs runs before they move
         old = 0 if self._a is None else int(self._a.shape[0])
         cap = max(self._capacity, 2 * old, rows)
         a = torch.empty(cap, self.n_layers, self.o_dim, dtype=torch.int8, device=self.device)
@@ -399,6 +402,7 @@ class DeviceLogitsCapture:
         self.device = torch.device(device)
         self._rows: Optional[torch.Tensor] = None
         self._n = 0
+        self.before_grow: Optional[Callable[[], None]] = None
 
     def __len__(self) -> int:
         return self._n
@@ -408,6 +412,8 @@ class DeviceLogitsCapture:
         if row.numel() != self.vocab:
             raise ValueError(f"logits row holds {row.numel()} values, vocab is {self.vocab}")
         if self._rows is None or self._n >= self._rows.shape[0]:
+            if self._rows is not None and self.before_grow is not None:
+                self.before_grow()
             old = 0 if self._rows is None else int(self._rows.shape[0])
             rows = torch.empty(max(self._capacity, 2 * old), self.vocab, dtype=torch.float32, device=self.device)
             if self._n:
@@ -459,3 +465,128 @@ def commit_captures(caps: DeviceCaptures, token_ids, prompt, sampling_seed, *, n
                             captured_logits_f32=logits, kv_cache=kv_cache, manifest=manifest,
                             x_attn=caps.x_attn if weight_provider is not None else None, scale_x_attn=sx,
                             weight_provider=weight_provider, ctx=ctx)
+
+
+class OnlineCapture:
+    """One request hashed while it decodes, straight from the device captures.
+
+    Joins :class:`DeviceCaptureBuffer` (and optionally
+    :class:`DeviceLogitsCapture`) to an
+    :class:`commitllm_b200.online.OnlineCommitter`: after each forward pass
+    and its sampling, :meth:`after_sampling` hands the pass's captured rows --
+    o_proj inputs and scales in place, the logits row of a generated token --
+    to the committer, which hashes the retained leaves and extends the IO
+    chain (now, or batched with later passes when deferred).  :meth:`finish`
+    builds the trace and IO trees, so after generation only the trees remain
+    (the reference hashes everything after generation,
+    crates/verilm-prover/src/lib.rs:336-499).  The roots equal those of
+    :func:`commit_captures` over the same captures.  Deferred passes address
+    the slabs, so a slab that has to grow first flushes the committer.
+    """
+
+    def __init__(self, buf: DeviceCaptureBuffer, committer, logits: Optional[DeviceLogitsCapture] = None,
+                 slot: int = 0):
+        self.buf, self.oc, self.logits, self.slot = buf, committer, logits, int(slot)
+        buf.before_grow = self._flush
+        if logits is not None:
+            logits.before_grow = self._flush
+        self._open = False
+
+    def _flush(self) -> None:
+        # hash the queued passes, and let the capturing stream reuse the old slab's
+        # memory only after the committer's stream has read it
+        import torch as _t
+        self.oc.flush()
+        if self.buf.device.type == "cuda":
+            _t.cuda.current_stream(self.buf.device).wait_stream(self.oc.ctx.stream)
+
+    def begin(self, prompt: bytes, sampling_seed: bytes, prompt_token_ids: Sequence[int]) -> None:
+        """Start the request (the prompt's token ids, as ``all_token_ids[:n_prompt]``)."""
+        if not prompt_token_ids:
+            raise ValueError("the prompt needs at least one token")
+        if self.buf._cursor or self.buf._calls:
+            raise RuntimeError("the capture buffer holds another request's captures: drain or reset it first")
+        self.oc.open(self.slot, prompt, sampling_seed, n_prompt_tokens=len(prompt_token_ids))
+        self.buf.reset_counter()
+        self.prompt_ids = [int(t) for t in prompt_token_ids]
+        self.n_prompt = len(self.prompt_ids)
+        self.done = 0
+        self._next_pass = 0
+        self._open = True
+
+    def after_sampling(self, next_token=None) -> None:
+        """Commit the rows of the forward pass(es) captured since the last call.
+        Row t commits ``all_token_ids[t + 1]``: a prompt token, or -- for the
+        last row of a pass that reached the end of the prompt -- the token just
+        sampled (``next_token``: an int or a one-element CUDA tensor; not
+        needed after a prefill chunk that ends inside the prompt)."""
+        import torch as _t
+        if not self._open:
+            raise RuntimeError("begin() first")
+        buf = self.buf
+        if buf._drift is not None:
+            raise RuntimeError(buf._drift)
+        if buf._calls % buf.calls_per_fwd != 0:
+            raise RuntimeError("after_sampling() between forward passes only")
+        t0, t1 = self.done, buf._cursor
+        n = t1 - t0
+        if n <= 0:
+            raise RuntimeError("no forward pass was captured since the last call")
+        from . import commit as C
+        dev = buf._a.device
+        L, H = buf.n_layers, buf.o_dim
+        # (pass, row) of the new tokens; the o_proj scale of row r of pass f, layer l
+        # is call f * 4L + 4l + O_PROJ_IDX of the request
+        rows = []
+        for f in range(self._next_pass, len(buf._fwd)):
+            rows += [(f, r) for r in range(buf._fwd[f])]
+        self._next_pass = len(buf._fwd)
+        a_rows, s_rows = [], []
+        for i, (f, r) in enumerate(rows):
+            t = t0 + i
+            a_rows.append([buf._a[t, l].data_ptr() for l in range(L)])
+            srow = []
+            for l in range(L):
+                k = f * buf.calls_per_fwd + PROJS_PER_LAYER * l + O_PROJ_IDX
+                sc = buf._scales[k]
+                if sc.dtype != _t.float32 or not sc.is_contiguous():
+                    sc = buf._scales[k] = sc.to(_t.float32).contiguous()
+                srow.append(sc.data_ptr() + 4 * r)
+            s_rows.append(srow)
+        lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[1] * n, tok_fwd=list(range(n)), tok_row=[0] * n,
+                            a_rows=a_rows, scale_a=s_rows, scale_stride=1)
+        gen_start = self.n_prompt - 1
+        if self.logits is not None and self.logits._rows is not None:
+            lay.logits = self.logits._rows
+            lay.tok_logits_row = [t - gen_start if gen_start <= t < gen_start + len(self.logits) else -1
+                                  for t in range(t0, t1)]
+        known = []
+        for t in range(t0, t1):
+            if t + 1 < self.n_prompt:
+                known.append(self.prompt_ids[t + 1])
+            elif t != t1 - 1:
+                raise RuntimeError("only the last row of a pass can commit a generated token")
+        ids = _t.tensor(known, dtype=_t.int32).to(dev, non_blocking=True) if known else None
+        if len(known) < n:
+            if next_token is None:
+                raise ValueError("this pass ends with a generated token: pass next_token")
+            last = (next_token.reshape(1).to(device=dev, dtype=_t.int32) if isinstance(next_token, _t.Tensor)
+                    else _t.tensor([int(next_token)], dtype=_t.int32).to(dev, non_blocking=True))
+            ids = _t.cat([ids, last]) if ids is not None else last
+        # the committer's stream reads what the model's stream captured
+        if dev.type == "cuda":
+            self.oc.ctx.stream.wait_stream(_t.cuda.current_stream(dev))
+        self.oc.step([self.slot] * n, lay, ids)
+        self.done = t1
+
+    def finish(self):
+        """Build the request's trees.  Returns ``(digests, captures)``: the
+        committer's device digests (``merkle_root``, ``io_root``, ...) and the
+        drained :class:`DeviceCaptures` (for the KV commit and later audits)."""
+        if not self._open:
+            raise RuntimeError("begin() first")
+        if self.done != self.buf._cursor:
+            raise RuntimeError("rows were captured after the last after_sampling()")
+        out = self.oc.close(self.slot)
+        self._open = False
+        return out, self.buf.drain()

@@ -210,3 +210,82 @@ def test_logits_capture_keeps_float32_rows():
     assert len(cap) == 0 and cap.drain().shape == (0, 10)
     with pytest.raises(ValueError):
         cap.capture(torch.zeros(11))
+
+
+class _FakeCommitter:
+    """Records what OnlineCapture hands an OnlineCommitter (CPU: no hashing)."""
+
+    def __init__(self):
+        self.steps, self.flushes, self.opened = [], 0, None
+        self.ctx = types.SimpleNamespace(device=None, stream=None)
+
+    def open(self, slot, prompt, seed, n_prompt_tokens=None):
+        self.opened = (slot, prompt, n_prompt_tokens)
+
+    def step(self, slots, layout, ids):
+        self.steps.append((list(slots), layout, ids.tolist()))
+
+    def flush(self):
+        self.flushes += 1
+
+    def close(self, slot):
+        return {"slot": slot, "n_tokens": sum(len(s[0]) for s in self.steps)}
+
+
+def test_online_capture_token_ids_and_rows():
+    """Row t of the request commits all_ids[t + 1]: prompt tokens from the
+    prompt, the last row of a pass that reaches the end of the prompt the
+    sampled token; logits rows bind from gen_start = n_prompt - 1; a growing
+    slab flushes the committer first."""
+    L, H, vocab = 2, 8, 5
+    buf = K.DeviceCaptureBuffer(L, H, capacity_tokens=3, device="cpu")
+    lg = K.DeviceLogitsCapture(vocab, capacity=1, device="cpu")
+    fc = _FakeCommitter()
+    onl = K.OnlineCapture(buf, fc, lg, slot=3)
+    prompt_ids = [11, 12, 13, 14, 15, 16]
+    onl.begin(b"p", bytes(32), prompt_ids)
+    assert fc.opened == (3, b"p", 6)
+    op = buf.wrap(lambda *a: None)
+
+    def run_pass(bs):
+        for _ in range(L * K.PROJS_PER_LAYER):
+            op(torch.zeros(bs, H, dtype=torch.int8), None, torch.ones(bs, 1), None)
+
+    run_pass(4)                                   # prefill chunk ending inside the prompt
+    onl.after_sampling()
+    assert fc.steps[-1][0] == [3] * 4 and fc.steps[-1][2] == [12, 13, 14, 15]
+    run_pass(2)                                   # the prompt's last two rows; the last one samples
+    lg.capture(torch.zeros(vocab))
+    with pytest.raises(ValueError, match="next_token"):
+        onl.after_sampling()
+    onl.after_sampling(21)
+    assert fc.steps[-1][2] == [16, 21]
+    assert fc.steps[-1][1].tok_logits_row == [-1, 0]
+    for tok in (22, 23):                          # decode steps
+        run_pass(1)
+        lg.capture(torch.zeros(vocab))
+        onl.after_sampling(tok)
+    assert [s[2] for s in fc.steps[2:]] == [[22], [23]]
+    assert [s[1].tok_logits_row for s in fc.steps[2:]] == [[1], [2]]
+    assert fc.flushes >= 2                        # the capture slab and the logits slab both grew
+    out, caps = onl.finish()
+    assert out["n_tokens"] == 8 and caps.n_tokens == 8
+    with pytest.raises(RuntimeError, match="begin"):
+        onl.after_sampling(1)
+
+
+def test_online_capture_refuses_a_dirty_buffer_and_a_partial_pass():
+    buf = K.DeviceCaptureBuffer(1, 4, device="cpu")
+    op = buf.wrap(lambda *a: None)
+    op(torch.zeros(1, 4, dtype=torch.int8), None, torch.ones(1, 1), None)
+    onl = K.OnlineCapture(buf, _FakeCommitter())
+    with pytest.raises(RuntimeError, match="drain or reset"):
+        onl.begin(b"p", bytes(32), [1, 2])
+    buf.reset()
+    buf.reset_counter()
+    onl.begin(b"p", bytes(32), [1, 2])
+    with pytest.raises(RuntimeError, match="no forward pass"):
+        onl.after_sampling(5)
+    op(torch.zeros(2, 4, dtype=torch.int8), None, torch.ones(2, 1), None)   # one call of a 4-call pass
+    with pytest.raises(RuntimeError, match="between forward passes"):
+        onl.after_sampling(5)

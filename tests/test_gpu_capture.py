@@ -161,3 +161,55 @@ def test_trailing_eos_pass_trimmed(ctx):
     h_host = V.commit_minimal_from_captures(o[:-L], s[: s.size - 4 * L], L, passes[:-1], ids[1:], PROMPT, SEED,
                                             n_prompt_tokens=6, captured_logits_f32=lg[:-1], ctx=ctx)
     assert h_dev.merkle_root_hex() == h_host.merkle_root_hex() and h_dev.io_root_hex() == h_host.io_root_hex()
+
+
+@pytest.mark.parametrize("defer", [0, 3, 8192])
+@pytest.mark.parametrize("chunks", [[9], [5, 4]], ids=["prefill", "chunked-prefill"])
+def test_online_capture_matches_the_offline_commit(ctx, defer, chunks):
+    """The request hashed pass by pass while it decodes (OnlineCapture) has the
+    roots of the offline commit of the same captures, and of the oracle.  Small
+    slabs make both the capture and the logits slab grow mid-request, which
+    flushes the deferred passes first."""
+    from commitllm_b200.online import OnlineCommitter
+    L, H, vocab, n_dec = 3, 256, 500, 12
+    n_prompt = sum(chunks)
+    dev = f"cuda:{ctx.device}"
+    buf = K.DeviceCaptureBuffer(L, H, capacity_tokens=4, device=dev)
+    lcap = K.DeviceLogitsCapture(vocab, capacity=2, device=dev)
+    oc = OnlineCommitter(ctx, max_slots=2, max_tokens=64, defer_tokens=defer)
+    onl = K.OnlineCapture(buf, oc, lcap, slot=1)
+    rng = np.random.default_rng(17 + defer + len(chunks))
+    all_ids = [int(x) for x in rng.integers(0, 32000, n_prompt + n_dec + 1)]
+    onl.begin(PROMPT, SEED, all_ids[:n_prompt])
+    g = torch.Generator(device=dev).manual_seed(99)
+    op = buf.wrap(lambda a, b, sa, sb, dt, bias: None)
+    host_o, host_s, host_lg = [], [], []
+    done = 0
+    for bs in chunks + [1] * n_dec:
+        for _l in range(L):
+            for p in range(K.PROJS_PER_LAYER):
+                a = torch.randint(-128, 128, (bs, H), generator=g, device=dev, dtype=torch.int8)
+                s = torch.rand(bs, 1, generator=g, device=dev) * 0.05 + 1e-3
+                op(a, None, s, None, torch.bfloat16, None)
+                if p == K.O_PROJ_IDX:
+                    host_o.append(a.cpu().numpy().reshape(-1))
+                host_s.append(s.cpu().numpy().reshape(-1))
+        done += bs
+        if done < n_prompt:
+            onl.after_sampling()                       # a prefill chunk: nothing sampled
+            continue
+        lg = (torch.randn(1, vocab, generator=g, device=dev) * 4).to(torch.bfloat16)
+        lcap.capture(lg)
+        host_lg.append(lg[0].float().cpu().numpy())
+        onl.after_sampling(torch.tensor([all_ids[done]], device=dev))
+    dig, caps = onl.finish()
+    logits = lcap.drain()
+    off = K.commit_captures(caps, all_ids[1:], PROMPT, SEED, n_prompt_tokens=n_prompt, logits=logits, ctx=ctx)
+    ctx.sync(20000)
+    assert bytes(dig["merkle_root"].cpu().numpy()).hex() == off.merkle_root_hex()
+    assert bytes(dig["io_root"].cpu().numpy()).hex() == off.io_root_hex()
+    retained = O.build_retained_from_captures([bytes(e) for e in host_o], np.concatenate(host_s), L,
+                                              chunks + [1] * n_dec)
+    com = O.commit_minimal(retained, all_ids[1:], PROMPT, SEED, captured_logits_f32=host_lg,
+                           n_prompt_tokens=n_prompt)
+    assert off.merkle_root_hex() == com.merkle_root.hex() and off.io_root_hex() == com.io_root.hex()

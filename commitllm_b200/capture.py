@@ -283,23 +283,27 @@ class DeviceCaptureBuffer:
         wrapped._device_capture = self
         return wrapped
 
-    def install(self, ops=None) -> None:
-        """Wrap ``ops.cutlass_scaled_mm`` (``vllm._custom_ops`` by default), as the
-        reference's ``register`` does (capture.py:982-1033)."""
+    def install(self, ops=None, name: str = "cutlass_scaled_mm") -> None:
+        """Wrap ``ops.<name>`` (``vllm._custom_ops.cutlass_scaled_mm`` by default),
+        as the reference's ``register`` does (capture.py:982-1033).  Any op with
+        the argument order (a, b, scale_a, scale_b, out_dtype, bias) can be
+        wrapped: vLLM's CUTLASS op refuses int8 on SM100, so an engine that runs
+        its W8A8 matmuls on B200 through another int8 GEMM installs the wrapper
+        on that op."""
         if self._installed is not None:
             raise RuntimeError("this capture buffer is already installed")
         if ops is None:
             import vllm._custom_ops as ops  # the serving engine's op table
-        cur = ops.cutlass_scaled_mm
+        cur = getattr(ops, name)
         if getattr(cur, "_device_capture", None) is not None:
-            raise RuntimeError("cutlass_scaled_mm is already wrapped by a capture buffer")
-        ops.cutlass_scaled_mm = self.wrap(cur)
-        self._installed = (ops, cur)
+            raise RuntimeError(f"{name} is already wrapped by a capture buffer")
+        setattr(ops, name, self.wrap(cur))
+        self._installed = (ops, name, cur)
 
     def uninstall(self) -> None:
         if self._installed is not None:
-            ops, cur = self._installed
-            ops.cutlass_scaled_mm = cur
+            ops, name, cur = self._installed
+            setattr(ops, name, cur)
             self._installed = None
 
     # --------------------------------------------------------------- requests

@@ -289,3 +289,25 @@ def test_online_capture_refuses_a_dirty_buffer_and_a_partial_pass():
     op(torch.zeros(2, 4, dtype=torch.int8), None, torch.ones(2, 1), None)   # one call of a 4-call pass
     with pytest.raises(RuntimeError, match="between forward passes"):
         onl.after_sampling(5)
+
+
+def test_configure_from_a_transformers_llama():
+    """The layer count and geometry of a real module tree (a tiny random
+    Llama from transformers), as configure_from_model reads them."""
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.LlamaConfig(num_hidden_layers=3, hidden_size=64, intermediate_size=128,
+                                   num_attention_heads=4, num_key_value_heads=2, vocab_size=100)
+    model = transformers.LlamaForCausalLM(cfg)
+    assert K.layer_count(model) == 3
+    buf = K.configure_from_model(model, device="cpu")
+    assert (buf.n_layers, buf.hidden, buf.o_dim, buf.calls_per_fwd) == (3, 64, 64, 12)
+
+
+def test_install_on_another_op():
+    ops = types.SimpleNamespace(int8_scaled_mm=lambda a, b, sa, sb, dt=None, bias=None: "other")
+    buf = K.DeviceCaptureBuffer(1, 4, device="cpu")
+    buf.install(ops, name="int8_scaled_mm")
+    for _ in range(4):
+        assert ops.int8_scaled_mm(torch.zeros(2, 4, dtype=torch.int8), None, torch.ones(2, 1), None) == "other"
+    buf.uninstall()
+    assert buf.drain().fwd_batch_sizes == [2]

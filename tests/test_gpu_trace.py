@@ -286,3 +286,43 @@ def test_c4_shape_retained_leaves_through_trace_plan(ctx):
         layers = [O.RetainedLayerState(a[k, l, s].tobytes(), float(sa[k, l, s]), x[k, l, s].tobytes(),
                                        float(sx[k, l, s])) for l in range(L)]
         assert got[i] == O.hash_retained_with_captured_logits(layers, None, None, logits[i])
+
+
+def test_trace_kernel_paths_agree_at_their_boundaries(ctx):
+    """vc_trace_leaves picks one of three kernels by token count (on 148 SMs:
+    the two-warp split kernel up to 2 x 148 x 32 = 9 472 tokens, the
+    one-thread kernel with a two-block prefetch below 3 x 148 CTAs of 128,
+    the busy kernel above).  The same tokens hashed through each give the same
+    leaves, mixed wraps in one warp included (every third token without
+    logits, every fifth with a final residual), and a sample of them equals
+    the oracle's."""
+    n_sm = torch.cuda.get_device_properties(ctx.device).multi_processor_count
+    L, H, V_ = 2, 200, 37
+    n_big = 3 * n_sm * 128 + 5                                   # busy kernel
+    g = torch.Generator(device=f"cuda:{ctx.device}").manual_seed(7)
+    dev = f"cuda:{ctx.device}"
+    a = torch.randint(-128, 128, (L, n_big, H), generator=g, device=dev, dtype=torch.int8)
+    sa = torch.rand(L, n_big, generator=g, device=dev)
+    lg = torch.randn(n_big, V_, generator=g, device=dev)
+    fr = torch.randn(n_big, 11, generator=g, device=dev)
+
+    def leaves(n):
+        lay = C.TraceLayout(n_layers=L, hidden=H, fwd_rows=[n], tok_fwd=[0] * n, tok_row=list(range(n)),
+                            a_rows=[[a[l].data_ptr() for l in range(L)]], scale_a=[[sa[l].data_ptr() for l in range(L)]],
+                            scale_stride=1, logits=lg, tok_logits_row=[t if t % 3 else -1 for t in range(n)],
+                            final_residual=fr, tok_fr_row=[t if t % 5 == 0 else -1 for t in range(n)])
+        out = C.trace_leaves(ctx, lay)
+        ctx.sync(60000)
+        return out.cpu().numpy()
+
+    n_split = 2 * n_sm * 32
+    l_split = leaves(n_split)
+    l_plain = leaves(n_split + 1)
+    l_busy = leaves(n_big)
+    assert np.array_equal(l_split, l_plain[:n_split]) and np.array_equal(l_plain, l_busy[: n_split + 1])
+    a_h, sa_h, lg_h, fr_h = a.cpu().numpy(), sa.cpu().numpy(), lg.cpu().numpy(), fr.cpu().numpy()
+    for t in (0, 1, 3, 5, 31, 32, n_split - 1, n_split, n_big - 1):
+        layers = [O.RetainedLayerState(a_h[l, t].tobytes(), float(sa_h[l, t])) for l in range(L)]
+        want = O.hash_retained_with_captured_logits(layers, fr_h[t] if t % 5 == 0 else None, None,
+                                                    lg_h[t] if t % 3 else None)
+        assert bytes(l_busy[t]) == want, t

@@ -386,9 +386,16 @@ def kv_commit_host(ctx: Context, k_host: Sequence[torch.Tensor], v_host: Sequenc
     n_groups = max(1, min(n_groups, L))
     bounds = [L * i // n_groups for i in range(n_groups + 1)]
     groups = []
-    cs.wait_stream(ctx.stream)     # the device buffers may still be read by earlier work
     for g in range(n_groups):
         lb, le = bounds[g], bounds[g + 1]
+        # a device buffer is overwritten once the hashing that last read it is done:
+        # each group's buffers carry the event of that launch (a buffer without one
+        # waits for everything queued on the context so far)
+        prior = {getattr(t, "_vc_read_done", None) for l in range(lb, le) for t in (dev_k[l], dev_v[l])}
+        if None in prior:
+            cs.wait_stream(ctx.stream)
+        for ev_prev in prior - {None}:
+            cs.wait_event(ev_prev)
         with torch.cuda.stream(cs):
             for l in range(lb, le):
                 dev_k[l].copy_(k_host[l], non_blocking=True)
@@ -405,6 +412,11 @@ def kv_commit_host(ctx: Context, k_host: Sequence[torch.Tensor], v_host: Sequenc
             r, ts = kv_commit(ctx, view, keep_trees=keep_trees, roots_out=ctx.empty(S, le - lb, 32))
             with torch.cuda.stream(ctx.stream):
                 roots_out[:, lb:le].copy_(r.view(S, le - lb, 32))
+        done = torch.cuda.Event()
+        done.record(ctx.stream)
+        for l in range(lb, le):
+            dev_k[l]._vc_read_done = done
+            dev_v[l]._vc_read_done = done
         if keep_trees:
             groups.append((lb, le, ts))
     return roots_out, (TreeGroups(groups, S) if keep_trees else None)

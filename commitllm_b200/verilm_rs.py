@@ -205,6 +205,15 @@ def _transcript_subset(inp: C.KvTranscriptInputs, layers: Sequence[int], n_pos: 
                                 per_channel=pick(inp.per_channel), biases=pick(inp.biases), rope=inp.rope)
 
 
+def _widen(rows: torch.Tensor) -> np.ndarray:
+    """K or V rows (bf16 / f32 / f64, or raw bf16 bits as int16 / uint16) as
+    f64 [n, kv_dim]: the KvEntry values hash_kv_entry hashes (exact widening)."""
+    r = rows.reshape(rows.shape[0], -1)
+    if r.dtype in (torch.int16, torch.uint16):
+        r = r.view(torch.bfloat16)
+    return r.to(torch.float64).numpy()
+
+
 def _f32_host(x) -> np.ndarray:
     if isinstance(x, torch.Tensor):
         x = x.detach().cpu().numpy()
@@ -258,6 +267,7 @@ class _Committed:
         self._kv_trees = kv_trees
         self._n_kv_layers = n_kv_layers
         self._kv_view = None
+        self._kv_host = None             # (K rows, V rows) per layer in host memory, after retain_kv("cpu")
         self._kvt = None                 # transcript inputs when the KV rows were recomputed and never stored
         self._host = None
 
@@ -347,6 +357,47 @@ class _Committed:
         return self._proof(self._kv_trees, layer, position)
 
     # --- KV openings of open_v4 (prover/src/lib.rs:1564-1588) ---
+    def retain_kv(self, device="cuda") -> None:
+        """Copy this request's K/V rows out of the cache the commit read, so
+        that later KV openings no longer depend on the engine keeping those
+        pages (the reference copies every ``KvEntry`` into its handle at
+        commit, prover/src/lib.rs:449-482).  The rows keep their dtype (bf16: a
+        quarter of the reference's f64 entries): on ``device`` (default the
+        commit's GPU, a contiguous ``[n_positions, n_kv_heads, head_dim]``
+        tensor per layer that openings read in place) or ``"cpu"`` (host
+        memory; openings widen the opened rows there).  Call it before the
+        engine reuses the request's pages.  A commitment whose K/V were
+        recomputed from x_attn holds its own inputs and needs none of this."""
+        view = self._kv_view
+        if view is None:
+            if self._kv_host is not None or self._kvt is not None:
+                return
+            raise ValueError("this commitment read no KV cache")
+        n = int(view.seq_lens[0])
+        dev = f"cuda:{self._ctx.device}"
+        ks, vs = [], []
+        with torch.cuda.stream(self._ctx.stream):
+            if view.block_tables is not None:
+                bs = int(view.k_layers[0].shape[1])
+                pos = torch.arange(n, device=dev)
+                page = view.block_tables[0].to(torch.long).index_select(0, pos // bs)
+                slot = pos % bs
+                for kl, vl in zip(view.k_layers, view.v_layers):
+                    ks.append(kl[page, slot].contiguous())
+                    vs.append(vl[page, slot].contiguous())
+            else:
+                off = int(view.seq_row_offset[0]) if view.seq_row_offset is not None else 0
+                for kl, vl in zip(view.k_layers, view.v_layers):
+                    # a copy even when the slice is already contiguous (.contiguous() would alias it)
+                    ks.append(kl[off:off + n].clone(memory_format=torch.contiguous_format))
+                    vs.append(vl[off:off + n].clone(memory_format=torch.contiguous_format))
+        if str(device) == "cpu":
+            self._ctx.sync()
+            self._kv_host = ([k.cpu() for k in ks], [v.cpu() for v in vs])
+            self._kv_view = None
+        else:
+            self._kv_view = C.KvCacheView(k_layers=ks, v_layers=vs, seq_lens=[n], layer_base=view.layer_base)
+
     def kv_openings(self, token_index: int, layer_indices: Optional[Sequence[int]] = None):
         """``(layers, entries f64 [n_sel, t+1, 2, kv_dim], siblings uint8 [n_sel, t+1, depth, 32])`` on the host.
 
@@ -358,11 +409,26 @@ class _Committed:
         """
         if self._kv_trees is None:
             raise ValueError("no KV transcript was committed")
-        n_pos = self._kv_view.seq_lens[0] if self._kv_view is not None else self._n_kv_positions()
+        if self._kv_host is not None:
+            n_pos = int(self._kv_host[0][0].shape[0])
+        elif self._kv_view is not None:
+            n_pos = self._kv_view.seq_lens[0]
+        else:
+            n_pos = self._n_kv_positions()
         if not 0 <= token_index < n_pos:
             raise ValueError(f"token_index {token_index} out of range")
         layers = list(range(self._n_kv_layers)) if layer_indices is None else [int(l) for l in layer_indices]
         layers = [l for l in layers if 0 <= l < self._n_kv_layers]   # open_v4 skips unknown layers
+        if self._kv_host is not None:
+            # rows retained in host memory: widen to f64 here (exact), proofs from the device trees
+            n = token_index + 1
+            if not layers:
+                return layers, np.zeros((0, n, 2, 0)), np.zeros((0, n, 0, 32), np.uint8)
+            ent = np.stack([np.stack([_widen(self._kv_host[0][l][:n]), _widen(self._kv_host[1][l][:n])], axis=1)
+                            for l in layers])
+            sib, depth = self._kv_trees.prove([l for l in layers for _ in range(n)], list(range(n)) * len(layers))
+            self._ctx.sync()
+            return layers, ent, sib.cpu().numpy()[:, : depth[0]].reshape(len(layers), n, depth[0], 32)
         if self._kvt is None:
             ent, sib, _ = C.kv_open(self._ctx, self._kv_view, self._kv_trees, 0, layers, token_index + 1)
             self._ctx.sync()

@@ -163,3 +163,57 @@ def test_commit_request_equals_the_from_captures_commit(ctx):
         r1 = R.zstd_decompress(h1.audit_v4_binary(t, layer_indices=[0])[4:])
         r2 = R.zstd_decompress(h2.audit_v4_binary(t, layer_indices=[0])[4:])
         assert r1 == r2
+
+
+@pytest.mark.parametrize("where", ["cuda", "cpu"])
+def test_retained_kv_survives_cache_reuse(ctx, where):
+    """After retain_kv, the receipts (KV entries and proofs included) do not
+    change when the engine overwrites the request's cache pages."""
+    import torch
+    h, _ = _commit(ctx)
+    before = {t: h.audit_v4_binary(t, layer_indices=[0, 1]) for t in (0, 9, C1["n_tokens"] - 1)}
+    cache = h._kv_view
+    h.retain_kv(where)
+    with torch.cuda.stream(ctx.stream):
+        for t in list(cache.k_layers) + list(cache.v_layers):
+            t.zero_()                       # the engine reuses the pages
+    ctx.sync()
+    for t, b in before.items():
+        assert h.audit_v4_binary(t, layer_indices=[0, 1]) == b
+    h.retain_kv(where)                      # a second call keeps what was retained
+    assert h.audit_v4_binary(9, layer_indices=[0, 1]) == before[9]
+
+
+def test_retained_kv_from_a_paged_cache(ctx):
+    """retain_kv gathers the rows of a paged cache (permuted pages): the
+    receipts before and after the pages are overwritten are identical, and
+    equal to those of the same request committed from a contiguous cache."""
+    import torch
+    from commitllm_b200.commit import KvCacheView
+    h_c, (k, v, tok, a, sc, logits) = _commit(ctx)
+    cont = h_c._kv_view
+    n, L, bs = C1["n_tokens"], C1["n_layers"], 16
+    nb = (n + bs - 1) // bs
+    perm = torch.randperm(nb + 3, generator=torch.Generator().manual_seed(3))[:nb]
+
+    def paged(t):
+        p = torch.zeros(nb + 3, bs, *t.shape[1:], dtype=t.dtype, device=t.device)
+        for b in range(nb):
+            rows = t[b * bs:(b + 1) * bs]
+            p[int(perm[b]), : rows.shape[0]] = rows
+        return p
+
+    view = KvCacheView([paged(t) for t in cont.k_layers], [paged(t) for t in cont.v_layers], [n],
+                       block_tables=perm.to(torch.int32).cuda(ctx.device)[None].contiguous())
+    h = V.commit_minimal_from_captures([a[t, l] for t in range(n) for l in range(L)], _drain_scales(L, [1] * n, sc),
+                                       L, [1] * n, [int(x) for x in tok], C1["prompt"].encode(),
+                                       bytes.fromhex(C1["sampling_seed"]), manifest=MANIFEST, n_prompt_tokens=3,
+                                       captured_logits_f32=logits, kv_cache=view, ctx=ctx)
+    assert h.kv_roots_hex() == h_c.kv_roots_hex()
+    want = h_c.audit_v4_binary(11, layer_indices=[0, 1])
+    h.retain_kv()
+    with torch.cuda.stream(ctx.stream):
+        for t in list(view.k_layers) + list(view.v_layers):
+            t.fill_(7)
+    ctx.sync()
+    assert h.audit_v4_binary(11, layer_indices=[0, 1]) == want

@@ -9,7 +9,10 @@ Same entry points, argument meanings and errors as
   ``manifest_hash_hex``, ``n_tokens``, ``kv_roots_hex`` (lib.rs:651-674).
 
 The hashing runs on the GPU through libvcommit; inputs may be host buffers
-(copied once to the device) or CUDA tensors (read in place).  KV roots come
+(copied once to the device, and owned by the handle) or CUDA tensors (read in
+place: the handle keeps them alive and its audits read them again, so they
+must not be overwritten while the handle is open; ``retain_kv`` copies a KV
+cache's rows out of the engine's pages).  KV roots come
 either, as in the reference, from ``compute_kv_transcript`` when both
 ``x_attn_inputs`` and a ``weight_provider`` are given (verilm-py/src/lib.rs:
 941-955; recomputed on the tensor cores from weights already on the GPU, see

@@ -270,6 +270,12 @@ class _Committed:
         self._kv_trees = kv_trees
         self._n_kv_layers = n_kv_layers
         self._kv_view = None
+        self._witnessed = None           # set_witnessed_scores: carried into the receipts
+        # accepted for the reference's interface (verilm-py/src/lib.rs:592-600): deep prefix openings
+        # need the bridge (RMSNorm) weights and shell openings, which this library does not build,
+        # so the receipts are those the reference gives without bridge weights (prefix_retained /
+        # prefix_shell_openings None)
+        self.deep_prefix = False
         self._kv_host = None             # (K rows, V rows) per layer in host memory, after retain_kv("cpu")
         self._kvt = None                 # transcript inputs when the KV rows were recomputed and never stored
         self._host = None
@@ -360,6 +366,23 @@ class _Committed:
         return self._proof(self._kv_trees, layer, position)
 
     # --- KV openings of open_v4 (prover/src/lib.rs:1564-1588) ---
+    def set_witnessed_scores(self, scores, n_q_heads: int) -> None:
+        """Attach witnessed attention scores, one flat row-major f32 array per
+        layer (``scores[qh * seq_len + t]``), carried into every receipt with
+        its KV openings (verilm-py/src/lib.rs:623-648; types.rs:1327-1334)."""
+        n_q_heads = int(n_q_heads)
+        if n_q_heads < 1:
+            raise ValueError("n_q_heads must be positive")
+        ws = []
+        for i, arr in enumerate(scores):
+            if isinstance(arr, torch.Tensor):
+                arr = arr.detach().float().cpu().numpy()
+            a = np.ascontiguousarray(np.asarray(arr, dtype=np.float32).ravel())
+            if a.size % n_q_heads:
+                raise ValueError(f"layer {i} score array length {a.size} not divisible by n_q_heads {n_q_heads}")
+            ws.append({"scores": a, "n_q_heads": n_q_heads, "seq_len": a.size // n_q_heads})
+        self._witnessed = ws
+
     def retain_kv(self, device="cuda") -> None:
         """Copy this request's K/V rows out of the cache the commit read, so
         that later KV openings no longer depend on the engine keeping those
@@ -537,7 +560,7 @@ class _Committed:
             "manifest": self._manifest, "prompt": self._prompt, "n_prompt_tokens": self._n_prompt_tokens,
             "output_text": output_text, "prefix_embedding_rows": None, "prefix_embedding_proofs": None,
             "prefix_retained": None, "prefix_shell_openings": None, "kv_entries": None, "kv_proofs": None,
-            "witnessed_scores": None,
+            "witnessed_scores": self._witnessed if include_kv else None,
         }
         if include_kv and self._kv_trees is not None:
             layers, ent, sib = self.kv_openings(i, layer_indices)
@@ -572,6 +595,9 @@ class MinimalBatchStateHandle(_Committed):
     def __init__(self, *a, x_attn=None, **k):
         super().__init__(*a, **k)
         self._x_attn = x_attn
+        # accepted for the reference's interface (lib.rs:603-611): it selects the x_attn of the
+        # shell opening, which this library does not build
+        self.use_captured_x_attn = False
 
     def has_captured_x_attn(self) -> bool:
         return self._x_attn is not None

@@ -217,3 +217,25 @@ def test_retained_kv_from_a_paged_cache(ctx):
             t.fill_(7)
     ctx.sync()
     assert h.audit_v4_binary(11, layer_indices=[0, 1]) == want
+
+
+def test_witnessed_scores_ride_in_the_receipt(ctx):
+    """set_witnessed_scores (verilm-py/src/lib.rs:623-648): the scores are in
+    every receipt that includes the KV openings, and absent otherwise."""
+    from commitllm_b200 import receipt as R
+    h, _ = _commit(ctx)
+    rng = np.random.default_rng(4)
+    scores = [rng.standard_normal(4 * 9).astype(np.float32) for _ in range(C1["n_layers"])]
+    h.set_witnessed_scores(scores, n_q_heads=4)
+    resp = R.deserialize_v4_audit(h.audit_v4_binary(8))
+    got = resp["witnessed_scores"]
+    assert len(got) == len(scores)
+    for g_, s in zip(got, scores):
+        assert g_["n_q_heads"] == 4 and g_["seq_len"] == 9 and np.array_equal(np.asarray(g_["scores"]), s)
+    assert R.deserialize_v4_audit(h.audit_v4_binary(8, include_kv=False))["witnessed_scores"] is None
+    assert json.loads(h.audit_v4(8))["witnessed_scores"][0]["seq_len"] == 9
+    with pytest.raises(ValueError, match="not divisible"):
+        h.set_witnessed_scores([np.zeros(10, np.float32)], n_q_heads=4)
+    assert h.deep_prefix is False and h.use_captured_x_attn is False
+    h.deep_prefix = True                     # accepted; no bridge weights here, as in the reference without them
+    assert R.deserialize_v4_audit(h.audit_v4_binary(8))["prefix_retained"] is None

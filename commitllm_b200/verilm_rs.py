@@ -6,7 +6,8 @@ Same entry points, argument meanings and errors as
 * :func:`commit_minimal_from_captures` (lib.rs:800-985)
 * :func:`commit_minimal_packed` (lib.rs:1189-1310)
 * handles with ``commitment_json``, ``merkle_root_hex``, ``io_root_hex``,
-  ``manifest_hash_hex``, ``n_tokens``, ``kv_roots_hex`` (lib.rs:651-674).
+  ``manifest_hash_hex``, ``n_tokens``, ``kv_roots_hex`` (lib.rs:651-674);
+* :class:`CaptureHook` (lib.rs:1842-1960).
 
 The hashing runs on the GPU through libvcommit; inputs may be host buffers
 (copied once to the device, and owned by the handle) or CUDA tensors (read in
@@ -688,6 +689,74 @@ def _wrap_rows(n_tokens, rows, n_prompt_tokens, which):
         gen_start = max(0, n_prompt_tokens - 1) if n_prompt_tokens is not None else 0
         return [t - gen_start if (t >= gen_start and t - gen_start < rows) else -1 for t in range(n_tokens)]
     return [t if t < rows else -1 for t in range(n_tokens)]
+
+
+class CaptureHook:
+    """The capture wrapper's bookkeeping (verilm-py/src/lib.rs:1842-1960): call
+    counting, per-call scale references and their drain, for a hook written
+    against ``verilm_rs.CaptureHook``.  ``drain_scales`` returns host numpy as
+    the reference does; ``drain_scales_device`` keeps the concatenated scales
+    on the device (``commit_minimal_from_captures`` reads CUDA scales in place).
+    :class:`commitllm_b200.capture.DeviceCaptureBuffer` is the whole device-side
+    hook."""
+
+    def __init__(self, calls_per_fwd: int, projs_per_layer: int, o_proj_idx: int = 1):
+        if calls_per_fwd < 1 or projs_per_layer < 1:
+            raise ValueError("calls_per_fwd and projs_per_layer must be positive")
+        self._calls_per_fwd, self._projs = int(calls_per_fwd), int(projs_per_layer)
+        self._counter = 0
+        self._minimal = 0
+        self._total = 0
+        self._scales: list = []
+
+    def record(self, scale_a) -> int:
+        """Keep the scale; return the call's projection index in its layer
+        (0 qkv, 1 o_proj, 2 gate_up, 3 down)."""
+        idx = self._counter % self._calls_per_fwd
+        self._counter += 1
+        self._scales.append(scale_a)
+        self._minimal += 1
+        self._total += 1
+        return idx % self._projs
+
+    def _cat(self):
+        try:
+            return torch.cat(self._scales)
+        except RuntimeError:                        # prefill [bs, 1] beside decode [1]: flatten each
+            return torch.cat([t.flatten() for t in self._scales])
+
+    def drain_scales(self):
+        """``(float32 numpy array, call count)`` of the scales recorded since the last drain."""
+        count, self._minimal = self._minimal, 0
+        if not self._scales:
+            return np.array([], dtype=np.float32), 0
+        cat = self._cat()
+        self._scales = []
+        return cat.detach().float().cpu().numpy().reshape(-1), count
+
+    def drain_scales_device(self):
+        """As :meth:`drain_scales`, the scales left on their device (no host copy)."""
+        count, self._minimal = self._minimal, 0
+        if not self._scales:
+            return torch.empty(0, dtype=torch.float32), 0
+        cat = self._cat()
+        self._scales = []
+        return cat.detach().to(torch.float32).reshape(-1), count
+
+    def reset_counter(self) -> None:
+        self._counter = 0
+
+    @property
+    def call_counter(self) -> int:
+        return self._counter
+
+    @property
+    def total_captured(self) -> int:
+        return self._total
+
+    @property
+    def minimal_call_count(self) -> int:
+        return self._minimal
 
 
 def commit_minimal_from_captures(o_proj_inputs, scales, n_layers, fwd_batch_sizes, token_ids, prompt,

@@ -311,3 +311,23 @@ def test_install_on_another_op():
         assert ops.int8_scaled_mm(torch.zeros(2, 4, dtype=torch.int8), None, torch.ones(2, 1), None) == "other"
     buf.uninstall()
     assert buf.drain().fwd_batch_sizes == [2]
+
+
+def test_verilm_rs_capture_hook_bookkeeping():
+    """verilm_rs.CaptureHook (verilm-py/src/lib.rs:1842-1960): projection index
+    by call counting, scales drained in call order (prefill [bs, 1] beside
+    decode [1]), counters."""
+    from commitllm_b200 import verilm_rs as V
+    hook = V.CaptureHook(calls_per_fwd=8, projs_per_layer=4, o_proj_idx=1)
+    seen = [hook.record(torch.full((3, 1), float(i))) for i in range(8)]          # a 3-row prefill pass
+    seen += [hook.record(torch.full((1,), float(8 + i))) for i in range(8)]       # a decode pass
+    assert seen == [0, 1, 2, 3] * 4
+    assert (hook.call_counter, hook.total_captured, hook.minimal_call_count) == (16, 16, 16)
+    arr, count = hook.drain_scales()
+    assert count == 16 and arr.dtype == np.float32
+    assert arr.tolist() == [float(i) for i in range(8) for _ in range(3)] + [float(8 + i) for i in range(8)]
+    assert hook.minimal_call_count == 0 and hook.drain_scales()[1] == 0
+    hook.reset_counter()
+    assert hook.record(torch.ones(1)) == 0 and hook.total_captured == 17
+    dev, count = hook.drain_scales_device()
+    assert count == 1 and isinstance(dev, torch.Tensor) and dev.tolist() == [1.0]
